@@ -1,0 +1,170 @@
+"""Decoder blocks on the fused sparse-conv path.
+
+* ``ResBlockStack`` -- chain of SparseResBlock3d
+  (burn_trellis/src/runtime_model/sparse_structure_decoder.rs:111-126):
+  ``x + conv2(SiLU(LN2(conv1(SiLU(LN1(x))))))``.  conv1's epilogue applies
+  LN2 + SiLU; conv2's epilogue adds the residual and, for every block but the
+  last, also emits the next block's SiLU(LN1(.)) as a second output, so each
+  block costs exactly two conv launches.
+* ``C2SUpsampleBlock`` -- the channel-to-space upsample of the TRELLIS.2
+  decoder (host order: sparse_decoder_runtime_impl.rs:1237-1345):
+  parents ``LN(g,b) -> SiLU -> SubM(Cin -> 8*Cout)``; conv1's epilogue writes
+  each kept child's channel block straight to its child row with
+  ``LN(no affine) -> SiLU`` applied (no [Np, 8*Cout] intermediate, no select);
+  conv2 on the children adds the repeat-interleaved parent skip in its
+  epilogue.
+* ``UpsamplePyramid``: levels of [C2S + ResBlocks].
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import flex_gmm as F
+
+RESBLOCK_LN_EPS = 1e-5  # sparse_structure_decoder.rs:22
+C2S_LN_EPS = 1e-6       # sparse_decoder.rs:43 (LAYER_NORM32_EPS)
+
+
+def _dev(a, device, dtype=None):
+    t = torch.as_tensor(np.ascontiguousarray(a), device=device)
+    return t.to(dtype) if dtype is not None else t
+
+
+@dataclass
+class ResBlockParams:
+    ln1_g: torch.Tensor
+    ln1_b: torch.Tensor
+    w1: torch.Tensor
+    b1: torch.Tensor
+    ln2_g: torch.Tensor
+    ln2_b: torch.Tensor
+    w2: torch.Tensor
+    b2: torch.Tensor
+    eps: float = RESBLOCK_LN_EPS
+
+    @staticmethod
+    def from_numpy(p: dict, device, dtype=torch.bfloat16) -> "ResBlockParams":
+        f32 = torch.float32
+        return ResBlockParams(_dev(p["ln1_g"], device, f32), _dev(p["ln1_b"], device, f32),
+                              _dev(p["w1"], device, dtype), _dev(p["b1"], device, f32),
+                              _dev(p["ln2_g"], device, f32), _dev(p["ln2_b"], device, f32),
+                              _dev(p["w2"], device, dtype), _dev(p["b2"], device, f32),
+                              float(p.get("eps", RESBLOCK_LN_EPS)))
+
+
+class ResBlockStack:
+    def __init__(self, blocks: list[ResBlockParams]):
+        self.blocks = blocks
+        c = blocks[0].w1.shape[0]
+        self.cfg = F.SparseSubmConvConfig.subm3(c, c)
+        self.channels = c
+
+    def conv_count(self) -> int:
+        return 2 * len(self.blocks)
+
+    def forward(self, x: torch.Tensor, nbr: torch.Tensor, bufs: dict | None = None) -> torch.Tensor:
+        """x [N, C] (bf16 or f32) -> [N, C]; ``nbr`` is the [N, 27] map."""
+        n, c = x.shape
+        if bufs is None:
+            bufs = {}
+        def buf(name):
+            t = bufs.get(name)
+            if t is None or t.shape != x.shape or t.dtype != x.dtype:
+                t = torch.empty_like(x)
+                bufs[name] = t
+            return t
+        b0 = self.blocks[0]
+        h = F.layer_norm_affine_silu_forward(x, b0.ln1_g, b0.ln1_b, b0.eps, out=buf("h"))
+        cur = x
+        ping = [buf("x0"), buf("x1")]
+        for i, p in enumerate(self.blocks):
+            h1 = F.sparse_subm_conv_forward(
+                self.cfg, h, nbr, p.w1, p.b1,
+                F.Epilogue(layer_norm=True, ln_eps=p.eps, ln_gamma=p.ln2_g, ln_beta=p.ln2_b, silu=True),
+                out=buf("h1"))
+            nxt = ping[i % 2]
+            if i + 1 < len(self.blocks):
+                q = self.blocks[i + 1]
+                e = F.Epilogue(residual=cur, layer_norm=True, ln_eps=q.eps, ln_gamma=q.ln1_g, ln_beta=q.ln1_b,
+                               silu=True, out2=h)
+            else:
+                e = F.Epilogue(residual=cur)
+            F.sparse_subm_conv_forward(self.cfg, h1, nbr, p.w2, p.b2, e, out=nxt)
+            cur = nxt
+        return cur
+
+
+@dataclass
+class C2SParams:
+    ln1_g: torch.Tensor
+    ln1_b: torch.Tensor
+    w1: torch.Tensor   # [8*Cout, 3, 3, 3, Cin]
+    b1: torch.Tensor
+    w2: torch.Tensor   # [Cout, 3, 3, 3, Cout]
+    b2: torch.Tensor
+
+    @staticmethod
+    def from_numpy(p: dict, device, dtype=torch.bfloat16) -> "C2SParams":
+        f32 = torch.float32
+        return C2SParams(_dev(p["ln1_g"], device, f32), _dev(p["ln1_b"], device, f32), _dev(p["w1"], device, dtype),
+                         _dev(p["b1"], device, f32), _dev(p["w2"], device, dtype), _dev(p["b2"], device, f32))
+
+
+class C2SUpsampleBlock:
+    def __init__(self, p: C2SParams):
+        self.p = p
+        self.cin = p.w1.shape[4]
+        self.cout = p.w2.shape[0]
+        self.cfg1 = F.SparseSubmConvConfig.subm3(self.cin, 8 * self.cout)
+        self.cfg2 = F.SparseSubmConvConfig.subm3(self.cout, self.cout)
+
+    def forward(self, coords: torch.Tensor, x: torch.Tensor, mask: torch.Tensor, nbr_parent=None):
+        """Returns (child_coords, child_feats, child_nbr)."""
+        p = self.p
+        h = F.layer_norm_affine_silu_forward(x, p.ln1_g, p.ln1_b, C2S_LN_EPS)
+        child_row, child_coords, skip_off = F.subdivide(coords, mask, self.cin)
+        n_child = child_coords.shape[0]
+        if nbr_parent is None:
+            nbr_parent = F.neighbor_rows_tensor_from_coords_tensor(self.cfg1, coords)
+        h_up = F.sparse_subm_conv_forward(
+            self.cfg1, h, nbr_parent, p.w1, p.b1,
+            F.Epilogue(layer_norm=True, ln_width=self.cout, ln_eps=C2S_LN_EPS, silu=True,
+                       out_row_map=child_row, out_row_map_cols=8),
+            out_rows=n_child)
+        nbr_child = F.neighbor_rows_tensor_from_coords_tensor(self.cfg2, child_coords)
+        rep = self.cout // (self.cin // 8)
+        y = F.sparse_subm_conv_forward(
+            self.cfg2, h_up, nbr_child, p.w2, p.b2,
+            F.Epilogue(residual=x, residual_offset=skip_off, residual_repeat=rep))
+        return child_coords, y, nbr_child
+
+    def flops(self, nbr_parent: torch.Tensor, nbr_child: torch.Tensor, mask: torch.Tensor) -> float:
+        """Algorithmic FLOPs: conv1 counted on kept children only (the
+        reference computes all 8 blocks, this path only kept ones)."""
+        kept = mask.to(torch.int64)
+        p_parent = (nbr_parent >= 0).sum(1).to(torch.int64)
+        f1 = 2.0 * float((p_parent[:, None] * kept).sum()) * self.cin * self.cout
+        f2 = 2.0 * float((nbr_child >= 0).sum()) * self.cout * self.cout
+        return f1 + f2
+
+
+class UpsamplePyramid:
+    """[C2S upsample + ResBlocks] x levels."""
+
+    def __init__(self, levels: list[dict], device, dtype=torch.bfloat16):
+        self.levels = []
+        for lv in levels:
+            self.levels.append((C2SUpsampleBlock(C2SParams.from_numpy(lv["c2s"], device, dtype)),
+                                ResBlockStack([ResBlockParams.from_numpy(r, device, dtype) for r in lv["res"]]),
+                                lv["mask_seed"]))
+
+    def forward(self, coords: torch.Tensor, x: torch.Tensor, masks: list[torch.Tensor]):
+        stats = []
+        for (c2s, res, _), mask in zip(self.levels, masks):
+            coords, x, nbr = c2s.forward(coords, x, mask)
+            x = res.forward(x, nbr)
+            stats.append((coords.shape[0], nbr))
+        return coords, x, stats

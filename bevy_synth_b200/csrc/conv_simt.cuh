@@ -1,0 +1,191 @@
+// conv_simt.cuh -- CUDA-core gather-GEMM for the sparse submanifold conv.
+//
+// The fp32 path (exact fp32 FFMA accumulation) and the fallback for shapes the
+// tensor-core kernel does not take (groups > 1, odd channel counts, K > 32).
+// Semantics follow the reference device kernels (burn_flex_gmm
+// src/wgpu/sparse_conv_kernels.rs:4-46 and the fused OC4 variants :89-337):
+// out[r, o] = bias[o] + sum_k sum_i in[nbr[r,k], g*Cin_g + i] * W[o, k, i],
+// invalid neighbors contribute nothing.  Instead of one thread per output
+// scalar re-reading its neighbor rows Cout times, a 64x64 output tile is
+// accumulated in registers (4x4 per thread) from 16-channel slices of the
+// gathered rows and the weights staged in shared memory; taps with no valid
+// row in the tile are skipped.
+#pragma once
+
+#include "sc_common.cuh"
+
+namespace sc {
+
+struct EpiParams {
+    const void* residual;
+    const int64_t* res_off;
+    int res_rep;
+    void* out;
+    const int32_t* row_map;
+    int map_cols;
+};
+
+template <typename T>
+__device__ __forceinline__ float load_residual(const T* res, const int64_t* res_off, int rep,
+                                               int64_t row, int col, int cout) {
+    if (res_off) return to_f32<T>(res[res_off[row] + col / rep]);
+    return to_f32<T>(res[row * (int64_t)cout + col]);
+}
+
+constexpr int SIMT_BM = 64, SIMT_BN = 64, SIMT_BK = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(256) conv_simt_kernel(
+    const T* __restrict__ in, int64_t n_in, int cin, int cin_g, const int32_t* __restrict__ nbr,
+    int64_t n_rows, int K, const T* __restrict__ w, const float* __restrict__ bias, int cout,
+    int cout_g, int blocks_per_group, EpiParams epi) {
+    __shared__ float As[SIMT_BK][SIMT_BM + 4];
+    __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
+    __shared__ int32_t nb_s[SIMT_BM];
+
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int64_t row0 = (int64_t)blockIdx.x * SIMT_BM;
+    const int group = blockIdx.y / blocks_per_group;
+    const int col0 = (blockIdx.y % blocks_per_group) * SIMT_BN;  // within the group
+    const int in_base = group * cin_g;
+    const int out_base = group * cout_g;
+
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+    for (int k = 0; k < K; ++k) {
+        int valid = 0;
+        if (tid < SIMT_BM) {
+            int64_t r = row0 + tid;
+            int32_t v = -1;
+            if (r < n_rows) {
+                v = __ldg(nbr + r * K + k);
+                if (v < -1 || v >= n_in) {
+                    raise_fault(FAULT_BAD_NEIGHBOR);
+                    v = -1;
+                }
+            }
+            nb_s[tid] = v;
+            valid = v >= 0;
+        }
+        if (!__syncthreads_or(valid)) continue;
+        for (int c0 = 0; c0 < cin_g; c0 += SIMT_BK) {
+            // A: 64 rows x 16 channels, 4 per thread
+            {
+                int r = tid >> 2, c = (tid & 3) * 4;
+                int32_t src = nb_s[r];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    float v = 0.f;
+                    if (src >= 0 && c0 + c + u < cin_g)
+                        v = to_f32<T>(in[(int64_t)src * cin + in_base + c0 + c + u]);
+                    As[c + u][r] = v;
+                }
+            }
+            // B: 64 output channels x 16 input channels of tap k
+            {
+                int o = tid >> 2, c = (tid & 3) * 4;
+                int oc = col0 + o;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    float v = 0.f;
+                    if (oc < cout_g && c0 + c + u < cin_g)
+                        v = to_f32<T>(w[((int64_t)(out_base + oc) * K + k) * cin_g + c0 + c + u]);
+                    Bs[c + u][o] = v;
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int kk = 0; kk < SIMT_BK; ++kk) {
+                float a[4], b[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+            }
+            __syncthreads();
+        }
+    }
+
+    // epilogue: bias, residual, scatter
+    const T* res = reinterpret_cast<const T*>(epi.residual);
+    T* out = reinterpret_cast<T*>(epi.out);
+    const int wb = epi.row_map ? cout / epi.map_cols : cout;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int64_t r = row0 + ty * 4 + i;
+        if (r >= n_rows) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int oc = col0 + tx * 4 + j;
+            if (oc >= cout_g) continue;
+            int o = out_base + oc;
+            float v = acc[i][j] + (bias ? bias[o] : 0.f);
+            if (res) v += load_residual<T>(res, epi.res_off, epi.res_rep, r, o, cout);
+            int64_t orow = r;
+            int ocol = o;
+            if (epi.row_map) {
+                orow = epi.row_map[r * epi.map_cols + o / wb];
+                ocol = o % wb;
+                if (orow < 0) continue;
+            }
+            out[orow * wb + ocol] = from_f32<T>(v);
+        }
+    }
+}
+
+// Row-wise LayerNorm (+affine) and/or SiLU over `width`-column groups.
+// Entry e addresses row map[e] (or e when map is null) of x/y, column block
+// (e % blocks_per_entry)...  Simplified: each entry is one row of `width`
+// values at element offset row*ld + col0.  Two-pass statistics as the
+// reference (sparse_decoder_wgpu_ops.rs:1642-1711): mean, then biased
+// variance sum((x-mean)^2)/C, inv_std = 1/sqrt(var + eps).
+template <typename T>
+__global__ void __launch_bounds__(256) rows_norm_act_kernel(
+    const T* __restrict__ x, T* __restrict__ y, int64_t n_entries, int width, int64_t ld,
+    const int32_t* __restrict__ row_map, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float eps, int do_ln, int do_silu) {
+    const int lane = threadIdx.x & 31;
+    int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (e >= n_entries) return;
+    int64_t row = row_map ? (int64_t)row_map[e] : e;
+    if (row < 0) return;
+    const T* xr = x + row * ld;
+    T* yr = y + row * ld;
+    float mean = 0.f, rstd = 1.f;
+    if (do_ln) {
+        float s = 0.f;
+        for (int c = lane; c < width; c += 32) s += to_f32<T>(xr[c]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        mean = s / (float)width;
+        float v = 0.f;
+        for (int c = lane; c < width; c += 32) {
+            float d = to_f32<T>(xr[c]) - mean;
+            v += d * d;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        rstd = 1.0f / sqrtf(v / (float)width + eps);
+    }
+    for (int c = lane; c < width; c += 32) {
+        float a = to_f32<T>(xr[c]);
+        if (do_ln) {
+            a = (a - mean) * rstd;
+            if (gamma) a *= gamma[c];
+            if (beta) a += beta[c];
+        }
+        if (do_silu) a = silu_f(a);
+        yr[c] = from_f32<T>(a);
+    }
+}
+
+}  // namespace sc

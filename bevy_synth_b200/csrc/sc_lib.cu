@@ -1,0 +1,500 @@
+// sc_lib.cu -- the C ABI of libsparseconv (declared in include/sparseconv.h).
+//
+// One translation unit: the kernels live in the *.cuh headers included here.
+// Host-side validation mirrors the reference's shape/dtype checks
+// (burn_flex_gmm src/lib.rs:698-725 validate_config; src/wgpu/sparse_conv.rs:
+// 369-473 validate_tensor_shapes) and reports them as SC_ERR_INVALID with a
+// message, as the reference returns Err(String).
+#include <cub/device/device_scan.cuh>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "conv_simt.cuh"
+#include "conv_tc.cuh"
+#include "neighbor.cuh"
+#include "rowops.cuh"
+#include "sc_common.cuh"
+
+namespace sc {
+
+thread_local std::string g_last_error;
+
+static int validate_config(const sc_conv_config* c) {
+    if (!c) return fail(SC_ERR_INVALID, "sparse conv config is null");
+    if (c->in_channels <= 0 || c->out_channels <= 0)
+        return fail(SC_ERR_INVALID, "sparse conv channel dimensions must be non-zero");
+    if (c->kernel_d <= 0 || c->kernel_h <= 0 || c->kernel_w <= 0)
+        return fail(SC_ERR_INVALID, "sparse conv kernel dimensions must be non-zero");
+    if (c->groups <= 0) return fail(SC_ERR_INVALID, "sparse conv groups must be non-zero");
+    if (c->in_channels_per_group * c->groups != c->in_channels)
+        return fail(SC_ERR_INVALID, "sparse conv in_channels/group mismatch");
+    if (c->out_channels_per_group * c->groups != c->out_channels)
+        return fail(SC_ERR_INVALID, "sparse conv out_channels/group mismatch");
+    bool used[3] = {false, false, false};
+    for (int i = 0; i < 3; ++i) {
+        int a = c->axis_order[i];
+        if (a < 0 || a > 2 || used[a])
+            return fail(SC_ERR_INVALID, "sparse conv axis_order must be a permutation of [0,1,2]");
+        used[a] = true;
+    }
+    return SC_OK;
+}
+
+static int64_t kernel_rows_of(const sc_conv_config* c) {
+    return c->kernel_d * c->kernel_h * c->kernel_w;
+}
+
+// kernel_layout (reference src/lib.rs:727-752)
+static void kernel_offsets_of(const sc_conv_config* c, int32_t* off) {
+    const int32_t cd = (int32_t)(c->kernel_d / 2), ch = (int32_t)(c->kernel_h / 2),
+                  cw = (int32_t)(c->kernel_w / 2);
+    int64_t k = 0;
+    for (int64_t kd = 0; kd < c->kernel_d; ++kd)
+        for (int64_t kh = 0; kh < c->kernel_h; ++kh)
+            for (int64_t kw = 0; kw < c->kernel_w; ++kw, ++k) {
+                const int32_t d[3] = {c->axis_sign[0] * ((int32_t)kd - cd),
+                                      c->axis_sign[1] * ((int32_t)kh - ch),
+                                      c->axis_sign[2] * ((int32_t)kw - cw)};
+                int32_t o[3] = {0, 0, 0};
+                o[c->axis_order[0]] = d[0];
+                o[c->axis_order[1]] = d[1];
+                o[c->axis_order[2]] = d[2];
+                off[3 * k] = o[0];
+                off[3 * k + 1] = o[1];
+                off[3 * k + 2] = o[2];
+            }
+}
+
+static inline unsigned grid1d(int64_t n, int block) { return (unsigned)((n + block - 1) / block); }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// --- TMA descriptor encoding through the driver entry point ------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+static bool force_simt() {
+    const char* e = std::getenv("SC_FORCE_SIMT");
+    return e && e[0] == '1';
+}
+
+struct TcPlan {
+    int tile_n, n_sub, sub_n, stages, grid_y;
+    uint32_t tmem_cols;
+    size_t smem;
+};
+
+static constexpr size_t kMaxDynSmem = 232448;  // 227 KB opt-in per block on sm_100
+
+// Decides whether the tensor-core kernel takes this conv and with which tiling.
+static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, TcPlan* plan) {
+    if (dt != SC_DTYPE_BF16 || c->groups != 1 || force_simt()) return false;
+    const int64_t K = kernel_rows_of(c), cin = c->in_channels, cout = c->out_channels;
+    if (K > TC_MAX_K || cin % 8 != 0 || cin < 64 || cout % 32 != 0) return false;
+    int tile_n;
+    if (e.d_out_row_map) {
+        if (e.out_row_map_cols <= 0 || cout % e.out_row_map_cols != 0) return false;
+        tile_n = (int)(cout / e.out_row_map_cols);
+        if (e.layer_norm && e.ln_width != 0 && e.ln_width != tile_n) return false;
+    } else if (e.layer_norm) {
+        const int64_t W = e.ln_width ? e.ln_width : cout;
+        if (cout <= 512)
+            tile_n = (int)cout;
+        else
+            tile_n = (int)W;
+        if (tile_n % W != 0 || cout % tile_n != 0) return false;
+    } else {
+        int64_t n_tiles = (cout + 255) / 256;
+        while (cout % n_tiles != 0 || (cout / n_tiles) % 32 != 0) ++n_tiles;
+        tile_n = (int)(cout / n_tiles);
+    }
+    if (tile_n > 512 || tile_n % 32 != 0) return false;
+    if (e.layer_norm) {
+        const int64_t W = e.ln_width ? e.ln_width : (e.d_out_row_map ? tile_n : cout);
+        if (W % 32 != 0 || tile_n % W != 0) return false;
+    }
+    plan->tile_n = tile_n;
+    plan->n_sub = tile_n > 256 ? 2 : 1;
+    plan->sub_n = tile_n / plan->n_sub;
+    if (plan->sub_n % 16 != 0) return false;
+    uint32_t cols = 32;
+    while (cols < (uint32_t)tile_n) cols <<= 1;
+    plan->tmem_cols = cols;
+    plan->grid_y = (int)(cout / tile_n);
+    const size_t fixed = 1024 + (size_t)TC_BM * K * 4 + 64 * 8 + 64;
+    const size_t stage = TC_A_BYTES + (size_t)tile_n * 128;
+    int S = (int)std::min<size_t>(6, (kMaxDynSmem - fixed) / stage);
+    if (S < 2) return false;
+    plan->stages = S;
+    plan->smem = fixed + S * stage;
+    return true;
+}
+
+static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, const int32_t* nbr,
+                     int64_t n_rows, const void* w, const float* bias, const sc_epilogue& e,
+                     void* out, cudaStream_t st, const TcPlan& plan) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const int64_t K = kernel_rows_of(c), cin = c->in_channels, cout = c->out_channels;
+    CUtensorMap wmap;
+    cuuint64_t dims[3] = {(cuuint64_t)cin, (cuuint64_t)K, (cuuint64_t)cout};
+    cuuint64_t strides[2] = {(cuuint64_t)cin * 2, (cuuint64_t)(K * cin * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)TC_BK, 1u, (cuuint32_t)plan.sub_n};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    CUresult r = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(w), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+
+    TcParams p;
+    memset(&p, 0, sizeof p);
+    p.in = static_cast<const __nv_bfloat16*>(in);
+    p.n_in = n_in;
+    p.cin = (int)cin;
+    p.nbr = nbr;
+    p.n_rows = n_rows;
+    p.K = (int)K;
+    p.bias = bias;
+    p.cout = (int)cout;
+    p.tile_n = plan.tile_n;
+    p.n_sub = plan.n_sub;
+    p.sub_n = plan.sub_n;
+    p.stages = plan.stages;
+    p.tmem_cols = plan.tmem_cols;
+    p.residual = static_cast<const __nv_bfloat16*>(e.d_residual);
+    p.res_off = e.d_residual_offset;
+    p.res_rep = e.residual_repeat > 0 ? e.residual_repeat : 1;
+    p.ln = e.layer_norm;
+    p.ln_width = e.layer_norm ? (e.ln_width ? e.ln_width : plan.tile_n) : plan.tile_n;
+    p.eps = e.ln_eps;
+    p.gamma = e.d_ln_gamma;
+    p.beta = e.d_ln_beta;
+    p.silu = e.silu;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.out2 = static_cast<__nv_bfloat16*>(e.d_out2);
+    p.row_map = e.d_out_row_map;
+    p.map_cols = e.d_out_row_map ? e.out_row_map_cols : 1;
+
+    static std::once_flag attr_once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once, [] {
+        attr_err = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)kMaxDynSmem);
+    });
+    SC_CUDA_TRY(attr_err);
+    dim3 grid((unsigned)((n_rows + TC_BM - 1) / TC_BM), (unsigned)plan.grid_y);
+    conv_tc_kernel<<<grid, TC_THREADS, plan.smem, st>>>(wmap, p);
+    SC_CUDA_TRY(cudaGetLastError());
+    return SC_OK;
+}
+
+template <typename T>
+static int launch_simt(const sc_conv_config* c, const void* in, int64_t n_in, const int32_t* nbr,
+                       int64_t n_rows, const void* w, const float* bias, const sc_epilogue& e,
+                       void* out, cudaStream_t st) {
+    const int64_t K = kernel_rows_of(c);
+    const int cout_g = (int)c->out_channels_per_group;
+    const int bpg = (cout_g + SIMT_BN - 1) / SIMT_BN;
+    EpiParams ep;
+    ep.residual = e.d_residual;
+    ep.res_off = e.d_residual_offset;
+    ep.res_rep = e.residual_repeat > 0 ? e.residual_repeat : 1;
+    ep.out = out;
+    ep.row_map = e.d_out_row_map;
+    ep.map_cols = e.d_out_row_map ? e.out_row_map_cols : 1;
+    dim3 grid(grid1d(n_rows, SIMT_BM), (unsigned)(bpg * c->groups));
+    conv_simt_kernel<T><<<grid, 256, 0, st>>>(
+        static_cast<const T*>(in), n_in, (int)c->in_channels, (int)c->in_channels_per_group, nbr,
+        n_rows, (int)K, static_cast<const T*>(w), bias, (int)c->out_channels, cout_g, bpg, ep);
+    SC_CUDA_TRY(cudaGetLastError());
+    if (e.layer_norm || e.silu) {
+        // post(y) as a second row pass over the stored y
+        const int64_t cout = c->out_channels;
+        int64_t width, ld, entries;
+        const int32_t* map = nullptr;
+        if (e.d_out_row_map) {
+            width = cout / e.out_row_map_cols;
+            ld = width;
+            entries = n_rows * e.out_row_map_cols;
+            map = e.d_out_row_map;
+        } else {
+            width = (e.layer_norm && e.ln_width) ? e.ln_width : cout;
+            ld = width;
+            entries = n_rows * (cout / width);
+        }
+        T* dst = static_cast<T*>(e.d_out2 ? e.d_out2 : out);
+        rows_norm_act_kernel<T><<<grid1d(entries * 32, 256), 256, 0, st>>>(
+            static_cast<const T*>(out), dst, entries, (int)width, ld, map, e.d_ln_gamma, e.d_ln_beta,
+            e.ln_eps, e.layer_norm, e.silu);
+        SC_CUDA_TRY(cudaGetLastError());
+    } else if (e.d_out2) {
+        const size_t bytes = (size_t)(e.d_out_row_map ? 0 : n_rows * c->out_channels) * sizeof(T);
+        if (e.d_out_row_map)
+            return fail(SC_ERR_UNSUPPORTED, "out2 without LayerNorm/SiLU is not supported with a row map");
+        SC_CUDA_TRY(cudaMemcpyAsync(e.d_out2, out, bytes, cudaMemcpyDeviceToDevice, st));
+    }
+    return SC_OK;
+}
+
+}  // namespace sc
+
+using namespace sc;
+
+extern "C" {
+
+int sc_version(void) { return 1; }
+
+int sc_last_error(char* buf, size_t len) {
+    const std::string& m = g_last_error;
+    if (buf && len) {
+        size_t n = std::min(len - 1, m.size());
+        memcpy(buf, m.data(), n);
+        buf[n] = 0;
+    }
+    return (int)m.size();
+}
+
+int sc_device_fault(uint32_t* h_fault) {
+    if (!h_fault) return fail(SC_ERR_INVALID, "h_fault is null");
+    SC_CUDA_TRY(cudaDeviceSynchronize());
+    SC_CUDA_TRY(cudaMemcpyFromSymbol(h_fault, g_fault, sizeof(uint32_t)));
+    const uint32_t zero = 0;
+    SC_CUDA_TRY(cudaMemcpyToSymbol(g_fault, &zero, sizeof(uint32_t)));
+    return SC_OK;
+}
+
+int sc_kernel_rows(const sc_conv_config* cfg, int64_t* rows) {
+    if (int rc = validate_config(cfg)) return rc;
+    if (!rows) return fail(SC_ERR_INVALID, "rows is null");
+    *rows = kernel_rows_of(cfg);
+    return SC_OK;
+}
+
+int sc_kernel_offsets(const sc_conv_config* cfg, int32_t* off) {
+    if (int rc = validate_config(cfg)) return rc;
+    if (!off) return fail(SC_ERR_INVALID, "offsets is null");
+    kernel_offsets_of(cfg, off);
+    return SC_OK;
+}
+
+int sc_neighbor_workspace_bytes(int64_t n_in, size_t* bytes) {
+    if (n_in < 0 || !bytes) return fail(SC_ERR_INVALID, "invalid neighbor workspace query");
+    *bytes = nb_workspace_bytes(n_in);
+    return SC_OK;
+}
+
+int sc_neighbor_map_query(const sc_conv_config* cfg, const int32_t* in_coords, int64_t n_in,
+                          const int32_t* q_coords, int64_t n_q, void* ws, size_t ws_bytes,
+                          int32_t* out, void* stream) {
+    if (int rc = validate_config(cfg)) return rc;
+    const int64_t K = kernel_rows_of(cfg);
+    if (K > kMaxKernelRows)
+        return fail(SC_ERR_UNSUPPORTED, "neighbor map supports at most 1024 kernel offsets");
+    if (cfg->kernel_d > 255 || cfg->kernel_h > 255 || cfg->kernel_w > 255)
+        return fail(SC_ERR_UNSUPPORTED, "neighbor map supports kernel extents up to 255");
+    if (n_in < 0 || n_q < 0) return fail(SC_ERR_INVALID, "negative row count");
+    if (n_in > 0x7ffffffeLL) return fail(SC_ERR_INVALID, "sparse conv coord row count exceeds i32::MAX");
+    if (!ws || ws_bytes < nb_workspace_bytes(n_in))
+        return fail(SC_ERR_CAPACITY, "neighbor workspace too small: need " +
+                                         std::to_string(nb_workspace_bytes(n_in)) + " bytes");
+    if ((n_in && !in_coords) || (n_q && (!q_coords || !out)))
+        return fail(SC_ERR_INVALID, "null coordinate or output pointer");
+    if (!aligned16(in_coords) || !aligned16(q_coords) || !aligned16(ws))
+        return fail(SC_ERR_INVALID, "coordinates and workspace must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint64_t cap = nb_capacity(n_in);
+    NbStatus* status = static_cast<NbStatus*>(ws);
+    HashSlot* table = reinterpret_cast<HashSlot*>(static_cast<uint8_t*>(ws) + 256);
+    SC_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(NbStatus), st));
+    SC_CUDA_TRY(cudaMemsetAsync(table, 0xff, cap * sizeof(HashSlot), st));
+    if (n_in > 0) {
+        nb_build_kernel<<<grid1d(n_in, 256), 256, 0, st>>>(reinterpret_cast<const int4*>(in_coords),
+                                                            n_in, table, cap - 1, status);
+        SC_CUDA_TRY(cudaGetLastError());
+    }
+    if (n_q > 0) {
+        KernelOffsets off;
+        off.k = (int32_t)K;
+        int32_t tmp[3 * kMaxKernelRows];
+        kernel_offsets_of(cfg, tmp);
+        for (int64_t i = 0; i < 3 * K; ++i) off.d[i] = (int8_t)tmp[i];
+        nb_query_kernel<<<grid1d(n_q * K, 256), 256, 0, st>>>(reinterpret_cast<const int4*>(q_coords),
+                                                               n_q, table, cap - 1, off, out);
+        SC_CUDA_TRY(cudaGetLastError());
+    }
+    return SC_OK;
+}
+
+int sc_neighbor_map(const sc_conv_config* cfg, const int32_t* coords, int64_t n, void* ws,
+                    size_t ws_bytes, int32_t* out, void* stream) {
+    return sc_neighbor_map_query(cfg, coords, n, coords, n, ws, ws_bytes, out, stream);
+}
+
+int sc_neighbor_status(const void* ws, int32_t* h_max_probe, void* stream) {
+    if (!ws) return fail(SC_ERR_INVALID, "workspace is null");
+    NbStatus h;
+    SC_CUDA_TRY(cudaMemcpyAsync(&h, ws, sizeof h, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
+    SC_CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    if (h_max_probe) *h_max_probe = h.max_probe;
+    if (h.bits & NB_STATUS_RANGE)
+        return fail(SC_ERR_RANGE, "sparse conv coordinate component outside [0, 65534]");
+    if (h.bits & NB_STATUS_CAPACITY) return fail(SC_ERR_CAPACITY, "neighbor hash table insert failed");
+    return SC_OK;
+}
+
+int sc_conv_uses_tensor_cores(const sc_conv_config* cfg, sc_dtype dtype, int32_t* flag) {
+    if (int rc = validate_config(cfg)) return rc;
+    if (!flag) return fail(SC_ERR_INVALID, "flag is null");
+    sc_epilogue e;
+    memset(&e, 0, sizeof e);
+    TcPlan plan;
+    *flag = plan_tc(cfg, dtype, e, &plan) ? 1 : 0;
+    return SC_OK;
+}
+
+int sc_subm_conv_forward(const sc_conv_config* cfg, sc_dtype dtype, const void* in, int64_t n_in,
+                         const int32_t* nbr, int64_t n_rows, const void* w, const float* bias,
+                         const sc_epilogue* epi, void* out, void* stream) {
+    if (int rc = validate_config(cfg)) return rc;
+    if (dtype != SC_DTYPE_F32 && dtype != SC_DTYPE_BF16)
+        return fail(SC_ERR_INVALID, "sparse conv dtype must be F32 or BF16");
+    if (n_rows < 0 || n_in < 0) return fail(SC_ERR_INVALID, "negative row count");
+    if (n_rows > n_in)
+        return fail(SC_ERR_INVALID, "sparse conv neighbor row count exceeds input rows: got " +
+                                        std::to_string(n_rows) + " input rows " + std::to_string(n_in));
+    sc_epilogue e;
+    if (epi)
+        e = *epi;
+    else
+        memset(&e, 0, sizeof e);
+    if (n_rows == 0) return SC_OK;
+    if (!in || !nbr || !w || !out) return fail(SC_ERR_INVALID, "null input, neighbor, weight or output pointer");
+    const int64_t cout = cfg->out_channels;
+    if (e.d_out_row_map && (e.out_row_map_cols <= 0 || cout % e.out_row_map_cols != 0))
+        return fail(SC_ERR_INVALID, "out_row_map_cols must divide out_channels");
+    if (e.layer_norm && e.ln_width < 0) return fail(SC_ERR_INVALID, "ln_width must be >= 0");
+    if (e.layer_norm && e.ln_width > 0 && cout % e.ln_width != 0)
+        return fail(SC_ERR_INVALID, "ln_width must divide out_channels");
+    if (e.layer_norm && e.d_out_row_map && e.ln_width && e.ln_width != cout / e.out_row_map_cols)
+        return fail(SC_ERR_INVALID, "with a row map, ln_width must equal the block width");
+    if (e.d_residual_offset && e.residual_repeat < 1)
+        return fail(SC_ERR_INVALID, "residual_repeat must be >= 1");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    TcPlan plan;
+    const bool al = aligned16(in) && aligned16(w) && aligned16(out) && aligned16(e.d_out2) &&
+                    aligned16(e.d_residual);
+    if (al && plan_tc(cfg, dtype, e, &plan))
+        return launch_tc(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st, plan);
+    if (dtype == SC_DTYPE_F32) return launch_simt<float>(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st);
+    return launch_simt<__nv_bfloat16>(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st);
+}
+
+int sc_layer_norm_act(sc_dtype dtype, const void* x, int64_t rows, int64_t channels, const float* gamma,
+                      const float* beta, float eps, int32_t ln, int32_t silu, void* y, void* stream) {
+    if (rows < 0 || channels <= 0) return fail(SC_ERR_INVALID, "invalid layer norm shape");
+    if (rows == 0) return SC_OK;
+    if (!x || !y) return fail(SC_ERR_INVALID, "null pointer");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (dtype == SC_DTYPE_F32)
+        rows_norm_act_kernel<float><<<grid1d(rows * 32, 256), 256, 0, st>>>(
+            static_cast<const float*>(x), static_cast<float*>(y), rows, (int)channels, channels, nullptr,
+            gamma, beta, eps, ln, silu);
+    else
+        rows_norm_act_kernel<__nv_bfloat16><<<grid1d(rows * 32, 256), 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), rows, (int)channels,
+            channels, nullptr, gamma, beta, eps, ln, silu);
+    SC_CUDA_TRY(cudaGetLastError());
+    return SC_OK;
+}
+
+int sc_bf16_round(const float* x, int64_t n, float* y, void* stream) {
+    if (n < 0) return fail(SC_ERR_INVALID, "negative length");
+    if (n == 0) return SC_OK;
+    bf16_round_kernel<<<grid1d(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, y);
+    SC_CUDA_TRY(cudaGetLastError());
+    return SC_OK;
+}
+
+int sc_cast(sc_dtype from, sc_dtype to, const void* x, int64_t n, void* y, void* stream) {
+    if (n < 0) return fail(SC_ERR_INVALID, "negative length");
+    if (n == 0) return SC_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (from == SC_DTYPE_F32 && to == SC_DTYPE_BF16)
+        cast_kernel<float, __nv_bfloat16><<<grid1d(n, 256), 256, 0, st>>>(
+            static_cast<const float*>(x), n, static_cast<__nv_bfloat16*>(y));
+    else if (from == SC_DTYPE_BF16 && to == SC_DTYPE_F32)
+        cast_kernel<__nv_bfloat16, float><<<grid1d(n, 256), 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(x), n, static_cast<float*>(y));
+    else
+        return fail(SC_ERR_INVALID, "unsupported cast");
+    SC_CUDA_TRY(cudaGetLastError());
+    return SC_OK;
+}
+
+static size_t subdiv_cub_bytes(int64_t n) {
+    size_t b = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, b, (const int32_t*)nullptr, (int32_t*)nullptr, (int)(n + 1));
+    return b;
+}
+
+int sc_subdivide_scratch_bytes(int64_t n_parent, size_t* bytes) {
+    if (n_parent < 0 || !bytes) return fail(SC_ERR_INVALID, "invalid subdivide scratch query");
+    const size_t a = ((size_t)(n_parent + 1) * 4 + 255) / 256 * 256;
+    *bytes = 2 * a + subdiv_cub_bytes(n_parent) + 256;
+    return SC_OK;
+}
+
+int sc_subdivide(const int32_t* parent_coords, const uint8_t* mask, int64_t n_parent,
+                 int64_t parent_channels, void* scratch, int32_t* child_row, int32_t* child_coords,
+                 int64_t* skip_offset, int64_t* h_children, void* stream) {
+    if (n_parent < 0 || !h_children) return fail(SC_ERR_INVALID, "invalid subdivide arguments");
+    if (n_parent * 8 > 0x7fffffffLL) return fail(SC_ERR_UNSUPPORTED, "too many parents for int32 child rows");
+    *h_children = 0;
+    if (n_parent == 0) return SC_OK;
+    if (!parent_coords || !mask || !scratch || !child_row)
+        return fail(SC_ERR_INVALID, "null pointer");
+    if (parent_channels % 8 != 0) return fail(SC_ERR_INVALID, "channel2spatial: in_channels is not divisible by 8");
+    if ((reinterpret_cast<uintptr_t>(mask) & 7u) != 0 || !aligned16(parent_coords) || !aligned16(child_coords))
+        return fail(SC_ERR_INVALID, "mask must be 8-byte and coordinates 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t a = ((size_t)(n_parent + 1) * 4 + 255) / 256 * 256;
+    int32_t* counts = static_cast<int32_t*>(scratch);
+    int32_t* offsets = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + a);
+    void* tmp = static_cast<uint8_t*>(scratch) + 2 * a;
+    size_t tmp_bytes = subdiv_cub_bytes(n_parent);
+    subdiv_count_kernel<<<grid1d(n_parent + 1, 256), 256, 0, st>>>(mask, n_parent, counts);
+    SC_CUDA_TRY(cudaGetLastError());
+    SC_CUDA_TRY(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, counts, offsets, (int)(n_parent + 1), st));
+    subdiv_write_kernel<<<grid1d(n_parent, 256), 256, 0, st>>>(
+        reinterpret_cast<const int4*>(parent_coords), mask, n_parent, parent_channels, offsets, child_row,
+        reinterpret_cast<int4*>(child_coords), skip_offset);
+    SC_CUDA_TRY(cudaGetLastError());
+    int32_t total = 0;
+    SC_CUDA_TRY(cudaMemcpyAsync(&total, offsets + n_parent, 4, cudaMemcpyDeviceToHost, st));
+    SC_CUDA_TRY(cudaStreamSynchronize(st));
+    *h_children = total;
+    return SC_OK;
+}
+
+}  // extern "C"

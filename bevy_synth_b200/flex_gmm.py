@@ -1,0 +1,323 @@
+"""Host-side mirror of the reference's sparse-conv operator API
+(mosure/bevy_synth, crate ``burn_flex_gmm``), backed by libsparseconv.so.
+
+Names, argument meaning and error behaviour follow the reference so that a
+caller of ``burn_flex_gmm`` finds the same operations:
+
+=============================================  ===============================================
+this module                                    reference (crates/burn_flex_gmm/...)
+=============================================  ===============================================
+``SparseSubmConvConfig``                       ``SparseSubmConvConfig`` (src/lib.rs:5-17)
+``kernel_rows`` / ``kernel_offsets``           ``kernel_rows`` / ``kernel_layout`` (lib.rs:59-67, 727-752)
+``neighbor_rows_tensor_from_coords_tensor``    same name (src/wgpu/neighbor.rs:977-1006)
+``neighbor_rows_query_tensor``                 chunked query (burn_trellis sparse_decoder_tests.rs:238-292)
+``sparse_subm_conv_forward_cubecl``            same name (src/wgpu/sparse_conv.rs:293-308)
+``sparse_subm_conv_forward``                   the above + the fused epilogue (``Epilogue``)
+``layer_norm_affine_forward``                  ``layer_norm_affine_forward_wgpu`` (src/wgpu/ops.rs:1464-1550)
+``layer_norm_affine_silu_forward``             ``layer_norm_affine_silu_forward_wgpu`` (ops.rs:1552-1639)
+``bf16_round_to_f32``                          ``bf16_round_to_f32_wgpu`` (src/wgpu.rs:69-102)
+=============================================  ===============================================
+
+Tensors are torch CUDA tensors (PyTorch is only the device-memory and stream
+plumbing); every computation runs in libsparseconv.  Errors are raised as
+``SparseConvError`` with the reference's messages where it has one.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from ._lib import DTYPE_BF16, DTYPE_F32, ScConvConfig, ScEpilogue, SparseConvError, check, lib
+
+INVALID_NEIGHBOR_ROW = -1
+
+
+@dataclass(frozen=True)
+class SparseSubmConvConfig:
+    in_channels: int
+    out_channels: int
+    kernel_d: int = 3
+    kernel_h: int = 3
+    kernel_w: int = 3
+    in_channels_per_group: int | None = None
+    out_channels_per_group: int | None = None
+    groups: int = 1
+    axis_order: tuple = (0, 1, 2)
+    axis_sign: tuple = (1, 1, 1)
+
+    def __post_init__(self):
+        if self.in_channels_per_group is None:
+            object.__setattr__(self, "in_channels_per_group", self.in_channels // max(self.groups, 1))
+        if self.out_channels_per_group is None:
+            object.__setattr__(self, "out_channels_per_group", self.out_channels // max(self.groups, 1))
+
+    def c(self) -> ScConvConfig:
+        return ScConvConfig(self.in_channels, self.out_channels, self.kernel_d, self.kernel_h, self.kernel_w,
+                            self.in_channels_per_group, self.out_channels_per_group, self.groups,
+                            (ctypes.c_int32 * 3)(*self.axis_order), (ctypes.c_int32 * 3)(*self.axis_sign))
+
+    @staticmethod
+    def subm3(in_channels: int, out_channels: int) -> "SparseSubmConvConfig":
+        """The decoder's 3x3x3, groups=1, identity-axis layer
+        (burn_trellis sparse_decoder_wgpu_ops.rs:1634-1640)."""
+        return SparseSubmConvConfig(in_channels, out_channels)
+
+
+def kernel_rows(config: SparseSubmConvConfig) -> int:
+    v = ctypes.c_int64(0)
+    c = config.c()
+    check(lib().sc_kernel_rows(ctypes.byref(c), ctypes.byref(v)))
+    return v.value
+
+
+def kernel_offsets(config: SparseSubmConvConfig) -> torch.Tensor:
+    K = kernel_rows(config)
+    out = torch.zeros((K, 3), dtype=torch.int32)
+    c = config.c()
+    check(lib().sc_kernel_offsets(ctypes.byref(c), ctypes.c_void_p(out.data_ptr())))
+    return out
+
+
+def _stream(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _require_cuda(name: str, t: torch.Tensor):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise SparseConvError(_lib.SC_ERR_INVALID, f"sparse conv {name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise SparseConvError(_lib.SC_ERR_INVALID, f"sparse conv {name} must be contiguous")
+
+
+def _coords_tensor(coords_t: torch.Tensor) -> torch.Tensor:
+    _require_cuda("coords", coords_t)
+    if coords_t.dim() != 2 or coords_t.shape[1] != 4:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv coords must have shape [N, 4], got {list(coords_t.shape)}")
+    if coords_t.dtype != torch.int32:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv coords dtype must be I32, got {coords_t.dtype}")
+    return coords_t
+
+
+class NeighborWorkspace:
+    """Caller-owned device workspace for the coordinate hash table."""
+
+    def __init__(self, device, n_in: int):
+        b = ctypes.c_size_t(0)
+        check(lib().sc_neighbor_workspace_bytes(n_in, ctypes.byref(b)))
+        self.bytes = b.value
+        self.buf = torch.empty(self.bytes, dtype=torch.uint8, device=device)
+
+    def status(self, device) -> int:
+        probe = ctypes.c_int32(0)
+        check(lib().sc_neighbor_status(_ptr(self.buf), ctypes.byref(probe),
+                                       ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)))
+        return probe.value
+
+
+def neighbor_rows_query_tensor(config: SparseSubmConvConfig, in_coords_t: torch.Tensor,
+                               query_coords_t: torch.Tensor, check_status: bool = True,
+                               workspace: NeighborWorkspace | None = None) -> torch.Tensor:
+    """[n_query, K] int32 rows of ``in_coords_t`` at query+offset (-1 absent)."""
+    _coords_tensor(in_coords_t)
+    _coords_tensor(query_coords_t)
+    K = kernel_rows(config)
+    n_in, n_q = in_coords_t.shape[0], query_coords_t.shape[0]
+    dev = in_coords_t.device
+    out = torch.empty((n_q, K), dtype=torch.int32, device=dev)
+    ws = workspace or NeighborWorkspace(dev, n_in)
+    c = config.c()
+    check(lib().sc_neighbor_map_query(ctypes.byref(c), _ptr(in_coords_t), n_in, _ptr(query_coords_t), n_q,
+                                      _ptr(ws.buf), ws.bytes, _ptr(out), _stream(in_coords_t)))
+    if check_status:
+        ws.status(dev)  # one host readback, as the reference's overflow check (neighbor.rs:859-879)
+    return out
+
+
+def neighbor_rows_tensor_from_coords_tensor(config: SparseSubmConvConfig, coords_t: torch.Tensor,
+                                            check_status: bool = True,
+                                            workspace: NeighborWorkspace | None = None) -> torch.Tensor:
+    """Device neighbor map [N, K] int32; duplicates resolve to the lowest row."""
+    return neighbor_rows_query_tensor(config, coords_t, coords_t, check_status, workspace)
+
+
+@dataclass
+class Epilogue:
+    """Fused conv epilogue (see sc_epilogue in include/sparseconv.h).
+
+    y = conv + bias (+ residual); ``out`` receives y when ``out2`` is given,
+    otherwise post(y) = [LayerNorm(gamma, beta)] -> [SiLU]."""
+
+    residual: torch.Tensor | None = None
+    residual_offset: torch.Tensor | None = None
+    residual_repeat: int = 1
+    layer_norm: bool = False
+    ln_width: int = 0
+    ln_eps: float = 1e-5
+    ln_gamma: torch.Tensor | None = None
+    ln_beta: torch.Tensor | None = None
+    silu: bool = False
+    out2: torch.Tensor | None = None
+    out_row_map: torch.Tensor | None = None
+    out_row_map_cols: int = 0
+    _keep: list = field(default_factory=list, repr=False)
+
+    def c(self) -> ScEpilogue:
+        return ScEpilogue(_ptr(self.residual), _ptr(self.residual_offset), int(self.residual_repeat),
+                          int(self.layer_norm), int(self.ln_width), float(self.ln_eps), _ptr(self.ln_gamma),
+                          _ptr(self.ln_beta), int(self.silu), _ptr(self.out2), _ptr(self.out_row_map),
+                          int(self.out_row_map_cols))
+
+
+_DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16}
+
+
+def _validate_conv(config, input, neighbor_rows, weight, bias):
+    """Mirror of validate_tensor_shapes (src/wgpu/sparse_conv.rs:369-473),
+    extended to bf16 (input and weight share the dtype; bias is f32)."""
+    for name, t in (("input", input), ("neighbor_rows", neighbor_rows), ("weight", weight)):
+        _require_cuda(name, t)
+    if input.dtype not in _DT:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv input dtype must be F32 or BF16 for kernel path, got {input.dtype}")
+    if weight.dtype != input.dtype:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv weight dtype must match input ({input.dtype}), got {weight.dtype}")
+    if bias is not None:
+        _require_cuda("bias", bias)
+        if bias.dtype != torch.float32:
+            raise SparseConvError(_lib.SC_ERR_INVALID,
+                                  f"sparse conv bias dtype must be F32 for kernel path, got {bias.dtype}")
+    if neighbor_rows.dtype != torch.int32:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv neighbor_rows dtype must be I32 for kernel path, got {neighbor_rows.dtype}")
+    if input.dim() != 2:
+        raise SparseConvError(_lib.SC_ERR_INVALID, f"sparse conv input rank mismatch: got {input.dim()} expected 2")
+    if neighbor_rows.dim() != 2:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv neighbor_rows rank mismatch: got {neighbor_rows.dim()} expected 2")
+    if weight.dim() != 5:
+        raise SparseConvError(_lib.SC_ERR_INVALID, f"sparse conv weight rank mismatch: got {weight.dim()} expected 5")
+    if input.shape[1] != config.in_channels:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv input channel mismatch: got {input.shape[1]} expected {config.in_channels}")
+    if neighbor_rows.shape[0] > input.shape[0]:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv neighbor row count exceeds input rows: got {neighbor_rows.shape[0]} "
+                              f"input rows {input.shape[0]}")
+    K = kernel_rows(config)
+    if neighbor_rows.shape[1] != K:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv neighbor kernel rows mismatch: got {neighbor_rows.shape[1]} expected {K}")
+    exp = [config.out_channels, config.kernel_d, config.kernel_h, config.kernel_w, config.in_channels_per_group]
+    if list(weight.shape) != exp:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv weight shape mismatch: got {list(weight.shape)} expected {exp}")
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != config.out_channels):
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"sparse conv bias len mismatch: got {bias.shape[0]} expected {config.out_channels}")
+
+
+def sparse_subm_conv_forward(config: SparseSubmConvConfig, input: torch.Tensor, neighbor_rows: torch.Tensor,
+                             weight: torch.Tensor, bias: torch.Tensor | None = None,
+                             epilogue: Epilogue | None = None, out: torch.Tensor | None = None,
+                             out_rows: int | None = None) -> torch.Tensor:
+    """Sparse submanifold conv with an optional fused epilogue.  Returns a new
+    contiguous [N_query, Cout] tensor (or ``out``) in the input's dtype."""
+    _validate_conv(config, input, neighbor_rows, weight, bias)
+    n_q = neighbor_rows.shape[0]
+    e = epilogue or Epilogue()
+    if out is None:
+        if e.out_row_map is not None:
+            width = config.out_channels // e.out_row_map_cols
+            rows = out_rows if out_rows is not None else n_q * e.out_row_map_cols
+            out = torch.empty((rows, width), dtype=input.dtype, device=input.device)
+        else:
+            out = torch.empty((n_q, config.out_channels), dtype=input.dtype, device=input.device)
+    c = config.c()
+    ec = e.c()
+    check(lib().sc_subm_conv_forward(ctypes.byref(c), _DT[input.dtype], _ptr(input), input.shape[0],
+                                     _ptr(neighbor_rows), n_q, _ptr(weight), _ptr(bias), ctypes.byref(ec),
+                                     _ptr(out), _stream(input)))
+    return out
+
+
+def sparse_subm_conv_forward_cubecl(config: SparseSubmConvConfig, input: torch.Tensor,
+                                    neighbor_rows: torch.Tensor, weight: torch.Tensor,
+                                    bias: torch.Tensor) -> torch.Tensor:
+    """The reference's device entry point (src/wgpu/sparse_conv.rs:293-308):
+    plain conv + bias, new output tensor."""
+    return sparse_subm_conv_forward(config, input, neighbor_rows, weight, bias)
+
+
+def uses_tensor_cores(config: SparseSubmConvConfig, dtype: torch.dtype) -> bool:
+    f = ctypes.c_int32(0)
+    c = config.c()
+    check(lib().sc_conv_uses_tensor_cores(ctypes.byref(c), _DT[dtype], ctypes.byref(f)))
+    return bool(f.value)
+
+
+def _layer_norm_act(x, gamma, beta, eps, ln, silu, out=None):
+    _require_cuda("input", x)
+    if x.dim() != 2:
+        raise SparseConvError(_lib.SC_ERR_INVALID, "layer norm input must be [rows, channels]")
+    y = out if out is not None else torch.empty_like(x)
+    check(lib().sc_layer_norm_act(_DT[x.dtype], _ptr(x), x.shape[0], x.shape[1], _ptr(gamma), _ptr(beta),
+                                  ctypes.c_float(eps), int(ln), int(silu), _ptr(y), _stream(x)))
+    return y
+
+
+def layer_norm_affine_forward(x, gamma=None, beta=None, eps: float = 1e-5, out=None):
+    return _layer_norm_act(x, gamma, beta, eps, True, False, out)
+
+
+def layer_norm_affine_silu_forward(x, gamma=None, beta=None, eps: float = 1e-5, out=None):
+    return _layer_norm_act(x, gamma, beta, eps, True, True, out)
+
+
+def silu_forward(x, out=None):
+    return _layer_norm_act(x, None, None, 0.0, False, True, out)
+
+
+def bf16_round_to_f32(x: torch.Tensor) -> torch.Tensor:
+    _require_cuda("input", x)
+    if x.dtype != torch.float32:
+        raise SparseConvError(_lib.SC_ERR_INVALID, "bf16_round_to_f32 expects an F32 tensor")
+    y = torch.empty_like(x)
+    check(lib().sc_bf16_round(_ptr(x), x.numel(), _ptr(y), _stream(x)))
+    return y
+
+
+def cast(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    _require_cuda("input", x)
+    y = torch.empty(x.shape, dtype=dtype, device=x.device)
+    check(lib().sc_cast(_DT[x.dtype], _DT[dtype], _ptr(x), x.numel(), _ptr(y), _stream(x)))
+    return y
+
+
+def subdivide(parent_coords: torch.Tensor, mask: torch.Tensor, parent_channels: int):
+    """Channel-to-space child expansion.  Returns (child_row [Np, 8] int32,
+    child_coords [Nc, 4] int32, skip_offset [Nc] int64)."""
+    _coords_tensor(parent_coords)
+    _require_cuda("mask", mask)
+    n = parent_coords.shape[0]
+    dev = parent_coords.device
+    b = ctypes.c_size_t(0)
+    check(lib().sc_subdivide_scratch_bytes(n, ctypes.byref(b)))
+    scratch = torch.empty(max(b.value, 1), dtype=torch.uint8, device=dev)
+    child_row = torch.empty((n, 8), dtype=torch.int32, device=dev)
+    coords = torch.empty((max(8 * n, 1), 4), dtype=torch.int32, device=dev)
+    skip = torch.empty(max(8 * n, 1), dtype=torch.int64, device=dev)
+    nc = ctypes.c_int64(0)
+    check(lib().sc_subdivide(_ptr(parent_coords), _ptr(mask), n, parent_channels, _ptr(scratch), _ptr(child_row),
+                             _ptr(coords), _ptr(skip), ctypes.byref(nc), _stream(parent_coords)))
+    k = nc.value
+    return child_row, coords[:k].contiguous(), skip[:k].contiguous()

@@ -1,0 +1,172 @@
+/*
+ * sparseconv.h -- C ABI of the B200 (sm_100a) sparse submanifold convolution
+ * library (libsparseconv.so).
+ *
+ * The entry points are what the reference's operator boundary would bind
+ * (mosure/bevy_synth, crate burn_flex_gmm, paths relative to the crate):
+ *
+ *   sc_neighbor_map        <- wgpu::neighbor_rows_tensor_from_coords_tensor
+ *                             (src/wgpu/neighbor.rs:977-1006)
+ *   sc_subm_conv_forward   <- wgpu::sparse_subm_conv_forward_cubecl
+ *                             (src/wgpu/sparse_conv.rs:293-308); the fused
+ *                             epilogue replaces the separate
+ *                             layer_norm_affine(_silu)_forward_wgpu passes
+ *                             (src/wgpu/ops.rs:1464-1639)
+ *   sc_layer_norm_act      <- wgpu::layer_norm_affine(_silu)_forward_wgpu
+ *                             (src/wgpu/ops.rs:1464-1639)
+ *   sc_bf16_round          <- wgpu::bf16_round_to_f32_wgpu (src/wgpu.rs:57-102)
+ *   sc_kernel_rows / sc_kernel_offsets
+ *                          <- kernel_rows / kernel_layout (src/lib.rs:59-67, 727-752)
+ *   sc_subdivide_*         <- burn_trellis decoder C2S helpers
+ *                             (runtime_model/sparse_decoder_wgpu_ops.rs:995-1054,
+ *                              1999-2076)
+ *
+ * Conventions (mirroring the reference's Result<_, String> boundary):
+ *  - Every function returns SC_OK (0) or a negative SC_ERR_* code; the message
+ *    of the last failure on the calling host thread is returned by
+ *    sc_last_error().
+ *  - Pointers named d_* are device pointers; h_* are host pointers.  Streams
+ *    are cudaStream_t passed as void*; nothing synchronises implicitly unless
+ *    documented (sc_neighbor_status, sc_device_fault).
+ *  - Inputs are never modified; outputs are caller-allocated.  Empty inputs
+ *    (zero rows) are valid and launch nothing.
+ *  - Coordinates are int32 [N,4] = (batch, x, y, z), row-major.
+ *  - Weights use the reference layout [Cout, KD, KH, KW, Cin/groups].
+ */
+#ifndef SPARSECONV_H
+#define SPARSECONV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SC_OK 0
+#define SC_ERR_INVALID (-1)     /* bad argument / shape (reference: Err(String)) */
+#define SC_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define SC_ERR_UNSUPPORTED (-3) /* valid request outside what this build implements */
+#define SC_ERR_CAPACITY (-4)    /* hash table full / probe limit / workspace too small */
+#define SC_ERR_RANGE (-5)       /* coordinate component outside [0, 65534] */
+#define SC_ERR_DEVICE (-6)      /* a kernel reported a fault (bounded wait expired,
+                                   neighbor index out of range) */
+
+typedef enum sc_dtype { SC_DTYPE_F32 = 0, SC_DTYPE_BF16 = 1 } sc_dtype;
+
+/* Mirror of SparseSubmConvConfig (src/lib.rs:5-17). */
+typedef struct sc_conv_config {
+    int64_t in_channels;
+    int64_t out_channels;
+    int64_t kernel_d, kernel_h, kernel_w;
+    int64_t in_channels_per_group;
+    int64_t out_channels_per_group;
+    int64_t groups;
+    int32_t axis_order[3];
+    int32_t axis_sign[3];
+} sc_conv_config;
+
+/* Fused epilogue of sc_subm_conv_forward.  With y = conv(x) + bias
+ * (+ residual), the call writes
+ *     out  = y                      when out2 != NULL, else  out = post(y)
+ *     out2 = post(y)                (optional)
+ * where post(y) = [LayerNorm over groups of ln_width columns, optional
+ * affine gamma/beta] then [SiLU], each step only if enabled.
+ * Zero-initialise the struct for "bias only". */
+typedef struct sc_epilogue {
+    const void* d_residual;        /* nullable; same dtype as out.  Element (i, j) is
+                                      d_residual[i*Cout + j], or, when d_residual_offset
+                                      is set, d_residual[d_residual_offset[i] + j / residual_repeat] */
+    const int64_t* d_residual_offset; /* nullable [n_rows] element offsets (C2S skip path) */
+    int32_t residual_repeat;       /* >= 1; channel repeat of the offset form */
+    int32_t layer_norm;            /* 0/1 */
+    int32_t ln_width;              /* LayerNorm group width in columns; 0 = Cout */
+    float ln_eps;
+    const float* d_ln_gamma;       /* nullable [ln_width] */
+    const float* d_ln_beta;        /* nullable [ln_width] */
+    int32_t silu;                  /* 0/1 */
+    void* d_out2;                  /* nullable second output, same dtype/shape as out */
+    const int32_t* d_out_row_map;  /* nullable [n_rows * out_row_map_cols]: scatter the
+                                      column block b (width Cout / out_row_map_cols) of row i
+                                      to output row d_out_row_map[i*cols + b] (skip if < 0);
+                                      the output then has row width Cout / cols */
+    int32_t out_row_map_cols;
+} sc_epilogue;
+
+/* ---- library / errors -------------------------------------------------- */
+int sc_version(void);
+/* Copies the calling thread's last error message; returns its length. */
+int sc_last_error(char* h_buf, size_t len);
+/* Reads and clears the sticky device fault word of the current device
+ * (synchronises the device).  0 = no fault. */
+int sc_device_fault(uint32_t* h_fault);
+
+/* ---- kernel layout ------------------------------------------------------- */
+int sc_kernel_rows(const sc_conv_config* cfg, int64_t* h_rows);
+int sc_kernel_offsets(const sc_conv_config* cfg, int32_t* h_offsets /* [K*3] */);
+
+/* ---- neighbor map ---------------------------------------------------------
+ * Builds a coordinate hash table from d_in_coords and answers, for every
+ * query row and kernel offset, the row of d_in_coords holding coord+offset
+ * (same batch), or -1.  Duplicate coordinates resolve to the LOWEST row, as
+ * every device builder of the reference does (src/wgpu/neighbor_kernels.rs:
+ * 37-39, 249-256).  Coordinate components must lie in [0, 65534]; a violation
+ * is recorded in the workspace status (SC_ERR_RANGE from sc_neighbor_status). */
+int sc_neighbor_workspace_bytes(int64_t n_in, size_t* h_bytes);
+int sc_neighbor_map(const sc_conv_config* cfg, const int32_t* d_coords, int64_t n_rows,
+                    void* d_workspace, size_t workspace_bytes, int32_t* d_neighbor_rows,
+                    void* stream);
+int sc_neighbor_map_query(const sc_conv_config* cfg, const int32_t* d_in_coords, int64_t n_in,
+                          const int32_t* d_query_coords, int64_t n_query, void* d_workspace,
+                          size_t workspace_bytes, int32_t* d_neighbor_rows, void* stream);
+/* Synchronises `stream`, then returns SC_OK or the error recorded by the
+ * last map built in this workspace (SC_ERR_RANGE / SC_ERR_CAPACITY).
+ * h_max_probe (nullable) receives the longest insert probe sequence. */
+int sc_neighbor_status(const void* d_workspace, int32_t* h_max_probe, void* stream);
+
+/* ---- convolution ----------------------------------------------------------
+ * out[n_rows, Cout] = bias + sum_k sum_c in[nbr[r,k], c] * W[o,k,c]  (+ epilogue)
+ * d_input [n_in, Cin], d_neighbor_rows [n_rows, K] (n_rows <= n_in is not
+ * required: query maps may address any input row < n_in), d_weight
+ * [Cout, KD, KH, KW, Cin/groups] in `dtype`, d_bias [Cout] fp32 (nullable =
+ * zero).  fp32 accumulates in fp32 FFMA; bf16 runs on tcgen05 tensor cores
+ * (fp32 accumulation in TMEM) when groups == 1, Cin % 8 == 0, Cout % 16 == 0
+ * and K <= 32, otherwise on a CUDA-core kernel.  Neighbor indices outside
+ * [-1, n_in) read as zero and raise the device fault word. */
+int sc_subm_conv_forward(const sc_conv_config* cfg, sc_dtype dtype, const void* d_input,
+                         int64_t n_in, const int32_t* d_neighbor_rows, int64_t n_rows,
+                         const void* d_weight, const float* d_bias, const sc_epilogue* epi,
+                         void* d_out, void* stream);
+
+/* Chooses the kernel family for a conv: 1 = tcgen05, 0 = CUDA cores. */
+int sc_conv_uses_tensor_cores(const sc_conv_config* cfg, sc_dtype dtype, int32_t* h_flag);
+
+/* ---- row ops ------------------------------------------------------------- */
+/* y = [SiLU]( LN(x) * gamma + beta ) over rows of `channels` (gamma/beta
+ * nullable); layer_norm = 0 skips the normalisation.  In-place allowed. */
+int sc_layer_norm_act(sc_dtype dtype, const void* d_x, int64_t rows, int64_t channels,
+                      const float* d_gamma, const float* d_beta, float eps, int32_t layer_norm,
+                      int32_t silu, void* d_y, void* stream);
+/* fp32 -> fp32 rounded to bf16 (RNE, no NaN special case). */
+int sc_bf16_round(const float* d_x, int64_t n, float* d_y, void* stream);
+/* fp32 <-> bf16 storage conversion (RNE). */
+int sc_cast(sc_dtype from, sc_dtype to, const void* d_x, int64_t n, void* d_y, void* stream);
+
+/* ---- channel-to-space subdivision (decoder upsample) ----------------------
+ * From a parent mask [n_parent, 8] (uint8, child c = cx + 2cy + 4cz), computes
+ * child_row[p*8 + c] (-1 where not kept) in parent-major / child-minor order,
+ * the child count, child coordinates (batch, 2x+cx, 2y+cy, 2z+cz) and the
+ * element offsets of the skip path (p*Cin + c*Cin/8).  d_scratch must hold
+ * sc_subdivide_scratch_bytes(n_parent) bytes.  h_children receives the count
+ * (this synchronises the stream, as the reference's argwhere count does). */
+int sc_subdivide_scratch_bytes(int64_t n_parent, size_t* h_bytes);
+int sc_subdivide(const int32_t* d_parent_coords, const uint8_t* d_mask, int64_t n_parent,
+                 int64_t parent_channels, void* d_scratch, int32_t* d_child_row,
+                 int32_t* d_child_coords /* [<= 8*n_parent, 4] */,
+                 int64_t* d_skip_offset /* [<= 8*n_parent] */, int64_t* h_children,
+                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPARSECONV_H */

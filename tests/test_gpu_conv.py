@@ -1,0 +1,256 @@
+"""Sparse submanifold conv on the GPU vs the CPU oracle.
+
+Tolerances: fp32 rel-L2 <= 1e-4 (and the reference's device-vs-CPU 1e-4
+max-abs bar, burn_flex_gmm/src/wgpu/tests.rs:1360-1503); bf16 rel-L2 <= 1e-2
+against the oracle run in fp32 on bf16-rounded inputs and weights."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from bevy_synth_b200 import _lib, synth
+from bevy_synth_b200 import flex_gmm as F
+
+from gpu_util import assert_no_fault, gpu_map, ocfg, rel_l2, to_dev
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+BF16 = torch.bfloat16
+
+
+def conv_gpu(cfg, coords, x, w, b, dtype=torch.float32, epi=None, nbr=None, **kw):
+    if nbr is None:
+        nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords.astype(np.int32)))
+    out = F.sparse_subm_conv_forward(cfg, to_dev(x, dtype), nbr, to_dev(w.reshape(cfg.out_channels, cfg.kernel_d,
+                                     cfg.kernel_h, cfg.kernel_w, cfg.in_channels_per_group), dtype),
+                                     to_dev(b, torch.float32), epi, **kw)
+    return out.float().cpu().numpy(), nbr
+
+
+def shell(grid=32, r=11.0, t=1.0, seed=0):
+    return synth.morton_sort(synth.unique_cells(0, synth.sphere_shell(grid, (grid / 2,) * 3, r, t)))
+
+
+def test_kat_uses_neighbor_voxels(cuda_device):
+    kat = json.load(open(os.path.join(GOLDEN, "kat_neighbor_voxels.json")))
+    cfg = F.SparseSubmConvConfig(1, 1, 3, 1, 1)
+    out, _ = conv_gpu(cfg, np.array(kat["coords"]), np.array(kat["input"], np.float32).reshape(2, 1),
+                      np.array(kat["weight"], np.float32), np.array(kat["bias"], np.float32))
+    np.testing.assert_allclose(out.reshape(-1), kat["expected"], atol=1e-5)
+    assert_no_fault()
+
+
+def lcg_case(seed, cfg, n_rows):
+    rng = oracle.Lcg(seed)
+    x = rng.take(n_rows * cfg.in_channels).reshape(n_rows, cfg.in_channels)
+    w = rng.take(cfg.out_channels * cfg.kernel_d * cfg.kernel_h * cfg.kernel_w * cfg.in_channels_per_group)
+    b = rng.take(cfg.out_channels)
+    return x, w, b
+
+
+def test_lcg_small_kernel_grouped(cuda_device):
+    cfg = F.SparseSubmConvConfig(4, 6, 3, 1, 1, groups=2)
+    coords = np.array([[0, i, 0, 0] for i in range(16)], np.int32)
+    x, w, b = lcg_case(42, cfg, 16)
+    out, _ = conv_gpu(cfg, coords, x, w, b)
+    exp = oracle.subm_conv_legacy(ocfg(cfg), w, b, coords.astype(np.uint32), x)
+    assert np.abs(out - exp).max() <= 1e-4
+
+
+@pytest.mark.parametrize("axis_order", [(0, 1, 2), (2, 1, 0), (1, 2, 0)])
+@pytest.mark.parametrize("axis_sign", [(1, 1, 1), (-1, 1, 1), (1, -1, -1)])
+def test_lcg_axis_permutations(cuda_device, axis_order, axis_sign):
+    coords = np.array([[0, x, y, z] for x in range(6) for y in range(5) for z in range(4)
+                       if (x + y + z) % 2 == 0], np.int32)
+    cfg = F.SparseSubmConvConfig(6, 8, groups=2, axis_order=axis_order, axis_sign=axis_sign)
+    x, w, b = lcg_case(991, cfg, coords.shape[0])
+    out, _ = conv_gpu(cfg, coords, x, w, b)
+    exp = oracle.subm_conv_legacy(ocfg(cfg), w, b, coords.astype(np.uint32), x)
+    assert np.abs(out - exp).max() <= 1e-4
+
+
+def test_config1_fp32_full(cuda_device):
+    wl = synth.config1(0)
+    cfg = F.SparseSubmConvConfig.subm3(64, 64)
+    out, nbr = conv_gpu(cfg, wl.coords, wl.feats, wl.params["w"], wl.params["b"])
+    exp = oracle.subm_conv_flex(ocfg(cfg), wl.params["w"], wl.params["b"], wl.feats, nbr.cpu().numpy(), threads=8)
+    assert rel_l2(out, exp) <= 1e-4
+    assert np.abs(out - exp).max() <= 1e-4
+    assert_no_fault()
+
+
+def bf16_ref(cfg, x, w, b, nbr):
+    return oracle.subm_conv_flex(ocfg(cfg), oracle.bf16_round(w), b, oracle.bf16_round(x), nbr, threads=8)
+
+
+@pytest.mark.parametrize("cin,cout", [(64, 64), (96, 96), (128, 256), (192, 192), (256, 256), (384, 384),
+                                      (512, 512), (768, 384), (64, 768), (256, 3072)])
+def test_bf16_tensor_core_widths(cuda_device, cin, cout):
+    coords = shell()
+    rng = np.random.default_rng(cin * 7 + cout)
+    x = rng.standard_normal((coords.shape[0], cin)).astype(np.float32)
+    w = (rng.standard_normal((cout, 3, 3, 3, cin)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    cfg = F.SparseSubmConvConfig.subm3(cin, cout)
+    assert F.uses_tensor_cores(cfg, BF16)
+    out, nbr = conv_gpu(cfg, coords, x, w, b, BF16)
+    exp = bf16_ref(cfg, x, w, b, nbr.cpu().numpy())
+    assert rel_l2(out, exp) <= 1e-2, rel_l2(out, exp)
+    assert rel_l2(out, exp) <= 4e-3
+    assert_no_fault()
+
+
+def test_bf16_row_tails_and_tap_skipping(cuda_device):
+    # rows far apart (only the centre tap valid) plus a dense clump; N % 128 != 0
+    rng = np.random.default_rng(5)
+    sparse = np.stack([np.zeros(77), rng.choice(20000, 77, replace=False) * 3,
+                       np.full(77, 5), np.full(77, 5)], 1).astype(np.int32)
+    clump = np.array([[0, x, y, z] for x in range(7) for y in range(7) for z in range(5)], np.int32) + \
+        np.array([0, 0, 100, 100], np.int32)
+    coords = np.concatenate([sparse, clump])
+    cfg = F.SparseSubmConvConfig.subm3(64, 128)
+    x = rng.standard_normal((coords.shape[0], 64)).astype(np.float32)
+    w = (rng.standard_normal((128, 3, 3, 3, 64)) * 0.05).astype(np.float32)
+    b = np.zeros(128, np.float32)
+    out, nbr = conv_gpu(cfg, coords, x, w, b, BF16)
+    assert rel_l2(out, bf16_ref(cfg, x, w, b, nbr.cpu().numpy())) <= 4e-3
+    assert_no_fault()
+
+
+def _epi_case(c=256, seed=1):
+    coords = shell(seed=seed)
+    rng = np.random.default_rng(seed)
+    n = coords.shape[0]
+    x = rng.standard_normal((n, c)).astype(np.float32)
+    w = (rng.standard_normal((c, 3, 3, 3, c)) * 0.02).astype(np.float32)
+    b = (0.1 * rng.standard_normal(c)).astype(np.float32)
+    res = rng.standard_normal((n, c)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(c)).astype(np.float32)
+    be = (0.1 * rng.standard_normal(c)).astype(np.float32)
+    return coords, x, w, b, res, g, be
+
+
+@pytest.mark.parametrize("force_simt", [False, True])
+def test_bf16_epilogue_ln_silu(cuda_device, force_simt, monkeypatch):
+    if force_simt:
+        monkeypatch.setenv("SC_FORCE_SIMT", "1")
+    coords, x, w, b, res, g, be = _epi_case()
+    cfg = F.SparseSubmConvConfig.subm3(256, 256)
+    epi = F.Epilogue(layer_norm=True, ln_eps=1e-5, ln_gamma=to_dev(g), ln_beta=to_dev(be), silu=True)
+    out, nbr = conv_gpu(cfg, coords, x, w, b, BF16, epi)
+    y = bf16_ref(cfg, x, w, b, nbr.cpu().numpy())
+    exp = oracle.silu(oracle.layer_norm(y, g, be, 1e-5))
+    assert rel_l2(out, exp) <= 1e-2
+    assert_no_fault()
+
+
+@pytest.mark.parametrize("force_simt", [False, True])
+def test_bf16_epilogue_residual_and_second_output(cuda_device, force_simt, monkeypatch):
+    if force_simt:
+        monkeypatch.setenv("SC_FORCE_SIMT", "1")
+    coords, x, w, b, res, g, be = _epi_case(seed=2)
+    cfg = F.SparseSubmConvConfig.subm3(256, 256)
+    out2 = torch.empty((coords.shape[0], 256), dtype=BF16, device="cuda:0")
+    epi = F.Epilogue(residual=to_dev(res, BF16), layer_norm=True, ln_eps=1e-5, ln_gamma=to_dev(g),
+                     ln_beta=to_dev(be), silu=True, out2=out2)
+    out, nbr = conv_gpu(cfg, coords, x, w, b, BF16, epi)
+    y = bf16_ref(cfg, x, w, b, nbr.cpu().numpy()) + oracle.bf16_round(res)
+    assert rel_l2(out, y) <= 1e-2
+    exp2 = oracle.silu(oracle.layer_norm(y, g, be, 1e-5))
+    assert rel_l2(out2.float().cpu().numpy(), exp2) <= 1e-2
+    assert_no_fault()
+
+
+def test_bf16_row_map_and_residual_offsets(cuda_device):
+    # C2S conv1 shape: Cin=128 -> 8 blocks of 64, scattered to child rows with
+    # per-block LayerNorm (no affine) + SiLU; then conv2 with the skip path.
+    coords = shell(grid=20, r=6.0)
+    n = coords.shape[0]
+    rng = np.random.default_rng(9)
+    cin, cc = 128, 64
+    x = rng.standard_normal((n, cin)).astype(np.float32)
+    w1 = (rng.standard_normal((8 * cc, 3, 3, 3, cin)) * 0.03).astype(np.float32)
+    b1 = np.zeros(8 * cc, np.float32)
+    mask = (rng.random((n, 8)) < 0.5).astype(np.uint8)
+    child_row, child_coords, skip = F.subdivide(to_dev(coords), to_dev(mask), cin)
+    oc, _ = oracle.channel2spatial(coords.astype(np.uint32), np.zeros((n, cin), np.float32), mask)
+    np.testing.assert_array_equal(child_coords.cpu().numpy(), oc.astype(np.int32))
+    nc = child_coords.shape[0]
+    cfg1 = F.SparseSubmConvConfig.subm3(cin, 8 * cc)
+    assert F.uses_tensor_cores(cfg1, BF16)
+    epi = F.Epilogue(layer_norm=True, ln_width=cc, ln_eps=1e-6, silu=True, out_row_map=child_row,
+                     out_row_map_cols=8)
+    out, nbr = conv_gpu(cfg1, coords, x, w1, b1, BF16, epi, out_rows=nc)
+    y1 = bf16_ref(cfg1, x, w1, b1, nbr.cpu().numpy())
+    _, hup = oracle.channel2spatial(coords.astype(np.uint32), y1, mask)
+    exp = oracle.silu(oracle.layer_norm(hup, None, None, 1e-6))
+    assert rel_l2(out, exp) <= 1e-2
+    # conv2 with the repeat-interleaved parent skip (rep = 64 / (128/8) = 4)
+    w2 = (rng.standard_normal((cc, 3, 3, 3, cc)) * 0.03).astype(np.float32)
+    cfg2 = F.SparseSubmConvConfig.subm3(cc, cc)
+    h_up = to_dev(out, BF16)
+    epi2 = F.Epilogue(residual=to_dev(x, BF16), residual_offset=skip, residual_repeat=4)
+    out2, nbr2 = conv_gpu(cfg2, child_coords.cpu().numpy(), out, w2, np.zeros(cc, np.float32), BF16, epi2)
+    _, xup = oracle.channel2spatial(coords.astype(np.uint32), oracle.bf16_round(x), mask)
+    exp2 = bf16_ref(cfg2, out, w2, np.zeros(cc, np.float32), nbr2.cpu().numpy()) + np.repeat(xup, 4, axis=1)
+    assert rel_l2(out2, exp2) <= 1e-2
+    assert_no_fault()
+
+
+def test_bf16_simt_fallback_grouped(cuda_device):
+    coords = shell(grid=16, r=5.0)
+    cfg = F.SparseSubmConvConfig.subm3(24, 40)
+    cfg = F.SparseSubmConvConfig(24, 40, groups=2)
+    assert not F.uses_tensor_cores(cfg, BF16)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((coords.shape[0], 24)).astype(np.float32)
+    w = rng.standard_normal((40, 3, 3, 3, 12)).astype(np.float32) * 0.1
+    b = rng.standard_normal(40).astype(np.float32)
+    out, nbr = conv_gpu(cfg, coords, x, w, b, BF16)
+    assert rel_l2(out, bf16_ref(cfg, x, w, b, nbr.cpu().numpy())) <= 1e-2
+
+
+def test_tensor_cores_agree_with_simt(cuda_device, monkeypatch):
+    coords = shell()
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((coords.shape[0], 192)).astype(np.float32)
+    w = (rng.standard_normal((192, 3, 3, 3, 192)) * 0.03).astype(np.float32)
+    b = np.zeros(192, np.float32)
+    cfg = F.SparseSubmConvConfig.subm3(192, 192)
+    tc, nbr = conv_gpu(cfg, coords, x, w, b, BF16)
+    monkeypatch.setenv("SC_FORCE_SIMT", "1")
+    simt, _ = conv_gpu(cfg, coords, x, w, b, BF16, nbr=nbr)
+    assert rel_l2(tc, simt) <= 5e-3
+
+
+def test_bad_neighbor_index_reads_zero_and_raises_fault(cuda_device):
+    cfg = F.SparseSubmConvConfig.subm3(64, 64)
+    coords = shell(grid=12, r=3.0)
+    n = coords.shape[0]
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords))
+    bad = nbr.clone()
+    bad[0, 0] = n + 1000  # outside [-1, n_in): the kernels' bounds check turns it into an error
+    x = to_dev(np.ones((n, 64), np.float32), BF16)
+    w = to_dev(np.zeros((64, 3, 3, 3, 64), np.float32), BF16)
+    F.sparse_subm_conv_forward(cfg, x, bad, w, None)
+    torch.cuda.synchronize()
+    assert _lib.device_fault() & 2
+    assert _lib.device_fault() == 0  # reading clears the word
+
+
+def test_full_size_config2_layer_sampled_rows(cuda_device):
+    """One C=256 layer at BASELINE config 2 size; a Morton-contiguous and a
+    random sample of rows checked against the oracle (size-independent)."""
+    wl = synth.config2(0, blocks=1)
+    cfg = F.SparseSubmConvConfig.subm3(256, 256)
+    p = wl.params[0]
+    out, nbr = conv_gpu(cfg, wl.coords, wl.feats, p["w1"], p["b1"], BF16)
+    nb = nbr.cpu().numpy()
+    rows = np.concatenate([np.arange(0, 2048), np.random.default_rng(0).choice(nb.shape[0], 2048, False)])
+    exp = oracle.subm_conv_flex(ocfg(cfg), oracle.bf16_round(p["w1"]), p["b1"], oracle.bf16_round(wl.feats),
+                                nb[rows], threads=8)
+    assert rel_l2(out[rows], exp) <= 4e-3
+    assert_no_fault()
