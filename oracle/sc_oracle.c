@@ -204,46 +204,63 @@ int oc_pack_flex_weight(const oc_conv_config* c, const float* w, float* packed) 
 }
 
 /* C[m,n] += A[m,k] @ B[k,n] for a row block; stands in for the single
- * matrixmultiply::sgemm call of lib.rs:347-366 (alpha = beta = 1).  A 4-row x
- * 32-column register tile; the full K extent is multiplied, zero-filled
- * (invalid) taps included, exactly as the reference's dense sgemm does. */
-static void gemm_accumulate(int64_t M, int64_t Kd, int64_t N, const float* A, int64_t lda,
-                            const float* B, int64_t ldb, float* C, int64_t ldc) {
-    int64_t m = 0;
-    for (; m + 4 <= M; m += 4) {
-        int64_t j = 0;
-        for (; j + 32 <= N; j += 32) {
-            float acc[4][32];
-            for (int r = 0; r < 4; ++r)
-                for (int x = 0; x < 32; ++x) acc[r][x] = 0.0f;
-            for (int64_t k = 0; k < Kd; ++k) {
-                const float* b = B + k * ldb + j;
-                float a0 = A[(m + 0) * lda + k], a1 = A[(m + 1) * lda + k];
-                float a2 = A[(m + 2) * lda + k], a3 = A[(m + 3) * lda + k];
-#pragma GCC unroll 32
-                for (int x = 0; x < 32; ++x) {
-                    acc[0][x] += a0 * b[x];
-                    acc[1][x] += a1 * b[x];
-                    acc[2][x] += a2 * b[x];
-                    acc[3][x] += a3 * b[x];
-                }
-            }
-            for (int r = 0; r < 4; ++r)
-                for (int x = 0; x < 32; ++x) C[(m + r) * ldc + j + x] += acc[r][x];
-        }
-        for (; j < N; ++j)
-            for (int r = 0; r < 4; ++r) {
-                float acc = 0.0f;
-                for (int64_t k = 0; k < Kd; ++k) acc += A[(m + r) * lda + k] * B[k * ldb + j];
-                C[(m + r) * ldc + j] += acc;
-            }
+ * matrixmultiply::sgemm call of lib.rs:347-366 (alpha = beta = 1), which is
+ * a packed, register-blocked SGEMM.  Here: K blocked by 256, a 6-row x
+ * 16-column AVX2/FMA register tile (12 accumulators), scalar edges.  The full
+ * K extent is multiplied, zero-filled (invalid) taps included, exactly as
+ * the reference's dense sgemm does. */
+#if defined(__AVX2__) && defined(__FMA__)
+#include <immintrin.h>
+static void tile_6x16(int64_t kc, const float* A, int64_t lda, const float* B, int64_t ldb,
+                      float* C, int64_t ldc) {
+    __m256 c00 = _mm256_setzero_ps(), c01 = _mm256_setzero_ps(), c10 = _mm256_setzero_ps(),
+           c11 = _mm256_setzero_ps(), c20 = _mm256_setzero_ps(), c21 = _mm256_setzero_ps(),
+           c30 = _mm256_setzero_ps(), c31 = _mm256_setzero_ps(), c40 = _mm256_setzero_ps(),
+           c41 = _mm256_setzero_ps(), c50 = _mm256_setzero_ps(), c51 = _mm256_setzero_ps();
+    for (int64_t k = 0; k < kc; ++k) {
+        const __m256 b0 = _mm256_loadu_ps(B + k * ldb), b1 = _mm256_loadu_ps(B + k * ldb + 8);
+        __m256 a;
+        a = _mm256_broadcast_ss(A + 0 * lda + k); c00 = _mm256_fmadd_ps(a, b0, c00); c01 = _mm256_fmadd_ps(a, b1, c01);
+        a = _mm256_broadcast_ss(A + 1 * lda + k); c10 = _mm256_fmadd_ps(a, b0, c10); c11 = _mm256_fmadd_ps(a, b1, c11);
+        a = _mm256_broadcast_ss(A + 2 * lda + k); c20 = _mm256_fmadd_ps(a, b0, c20); c21 = _mm256_fmadd_ps(a, b1, c21);
+        a = _mm256_broadcast_ss(A + 3 * lda + k); c30 = _mm256_fmadd_ps(a, b0, c30); c31 = _mm256_fmadd_ps(a, b1, c31);
+        a = _mm256_broadcast_ss(A + 4 * lda + k); c40 = _mm256_fmadd_ps(a, b0, c40); c41 = _mm256_fmadd_ps(a, b1, c41);
+        a = _mm256_broadcast_ss(A + 5 * lda + k); c50 = _mm256_fmadd_ps(a, b0, c50); c51 = _mm256_fmadd_ps(a, b1, c51);
     }
-    for (; m < M; ++m)
-        for (int64_t j = 0; j < N; ++j) {
+#define ACC(r, lo, hi)                                                                        \
+    _mm256_storeu_ps(C + r * ldc, _mm256_add_ps(_mm256_loadu_ps(C + r * ldc), lo));           \
+    _mm256_storeu_ps(C + r * ldc + 8, _mm256_add_ps(_mm256_loadu_ps(C + r * ldc + 8), hi));
+    ACC(0, c00, c01) ACC(1, c10, c11) ACC(2, c20, c21) ACC(3, c30, c31) ACC(4, c40, c41) ACC(5, c50, c51)
+#undef ACC
+}
+#endif
+
+static void gemm_edge(int64_t m0, int64_t m1, int64_t n0, int64_t n1, int64_t k0, int64_t kc,
+                      const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc) {
+    for (int64_t m = m0; m < m1; ++m)
+        for (int64_t j = n0; j < n1; ++j) {
             float acc = 0.0f;
-            for (int64_t k = 0; k < Kd; ++k) acc += A[m * lda + k] * B[k * ldb + j];
+            for (int64_t k = k0; k < k0 + kc; ++k) acc += A[m * lda + k] * B[k * ldb + j];
             C[m * ldc + j] += acc;
         }
+}
+
+static void gemm_accumulate(int64_t M, int64_t Kd, int64_t N, const float* A, int64_t lda,
+                            const float* B, int64_t ldb, float* C, int64_t ldc) {
+    const int64_t KC = 256;
+    for (int64_t k0 = 0; k0 < Kd; k0 += KC) {
+        const int64_t kc = Kd - k0 < KC ? Kd - k0 : KC;
+#if defined(__AVX2__) && defined(__FMA__)
+        const int64_t M6 = M - M % 6, N16 = N - N % 16;
+        for (int64_t j = 0; j < N16; j += 16)
+            for (int64_t m = 0; m < M6; m += 6)
+                tile_6x16(kc, A + m * lda + k0, lda, B + k0 * ldb + j, ldb, C + m * ldc + j, ldc);
+        gemm_edge(M6, M, 0, N, k0, kc, A, lda, B, ldb, C, ldc);
+        gemm_edge(0, M6, N16, N, k0, kc, A, lda, B, ldb, C, ldc);
+#else
+        gemm_edge(0, M, 0, N, k0, kc, A, lda, B, ldb, C, ldc);
+#endif
+    }
 }
 
 /* lib.rs:242-375 (sparse_subm_conv_forward_flex_precomputed).
