@@ -214,13 +214,16 @@ def main():
     stream = torch.cuda.current_stream(dev)
     conv_events: list = []
 
+    use_order = os.environ.get("SC_ROW_ORDER", "1") == "1"
+
     def step(coords_t, feats_t, record=False):
         nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, coords_t, check_status=False, workspace=ws)
+        order = F.neighbor_schedule(cfg, nbr) if use_order else None
         if record:
-            return stack_forward_timed(feats_t, nbr)
-        return stack.forward(feats_t, nbr, bufs), nbr
+            return stack_forward_timed(feats_t, nbr, order)
+        return stack.forward(feats_t, nbr, bufs, order), nbr
 
-    def stack_forward_timed(x, nbr):
+    def stack_forward_timed(x, nbr, order):
         # identical to ResBlockStack.forward, with events around each conv launch
         b0 = stack.blocks[0]
         h = F.layer_norm_affine_silu_forward(x, b0.ln1_g, b0.ln1_b, b0.eps, out=bufs["h"])
@@ -231,16 +234,16 @@ def main():
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             F.sparse_subm_conv_forward(cfg, h, nbr, p.w1, p.b1, F.Epilogue(layer_norm=True, ln_eps=p.eps,
-                                       ln_gamma=p.ln2_g, ln_beta=p.ln2_b, silu=True), out=h1)
+                                       ln_gamma=p.ln2_g, ln_beta=p.ln2_b, silu=True, schedule=order), out=h1)
             e1.record(stream)
             conv_events.append((e0, e1))
             nxt = ping[i % 2]
             if i + 1 < len(stack.blocks):
                 q = stack.blocks[i + 1]
                 e = F.Epilogue(residual=cur, layer_norm=True, ln_eps=q.eps, ln_gamma=q.ln1_g, ln_beta=q.ln1_b,
-                               silu=True, out2=h)
+                               silu=True, out2=h, schedule=order)
             else:
-                e = F.Epilogue(residual=cur)
+                e = F.Epilogue(residual=cur, schedule=order)
             e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e2.record(stream)
             F.sparse_subm_conv_forward(cfg, h1, nbr, p.w2, p.b2, e, out=nxt)
@@ -335,7 +338,8 @@ def main():
             "tflops": tflops, "pct_bf16_peak": tflops / peak_tf,
             "config": {"workload": wl.name, "voxels_per_gpu": n, "voxels_total": n_all, "blocks": len(wl.params),
                        "channels": c, "convs_per_step": convs, "valid_pairs_P": P,
-                       "step": "neighbor map + LN1/SiLU + 8 fused SubM convs",
+                       "step": "neighbor map + row order + LN1/SiLU + 8 fused SubM convs",
+                       "row_order": "mask-sorted" if use_order else "morton",
                        "l2": "flushed before every step (256 MiB write); per-step CUDA events",
                        "parallelism": f"asset-sharded x{world} (one independent asset per GPU, no collective)"},
             "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
@@ -346,7 +350,7 @@ def main():
             "e2e": {"value": units / t_e2e, "unit": "voxel-outputs/s",
                     "h2d_bytes_per_step": int(coords_h.numel() * 4 + feats_h.numel() * 2),
                     "d2h_bytes_per_step": int(out_h.numel() * 2)},
-            "gpu_launches": int(args.steps * (2 + 1 + convs)),
+            "gpu_launches": int(args.steps * (2 + (2 if use_order else 0) + 1 + convs)),
             "clocks": sampler.report(),
         }
         print(json.dumps(line), flush=True)

@@ -27,6 +27,7 @@ DTYPE_BF16 = 1
 EXPORTED = (
     "sc_version", "sc_last_error", "sc_device_fault", "sc_kernel_rows", "sc_kernel_offsets",
     "sc_neighbor_workspace_bytes", "sc_neighbor_map", "sc_neighbor_map_query", "sc_neighbor_status",
+    "sc_neighbor_schedule_scratch_bytes", "sc_neighbor_schedule",
     "sc_subm_conv_forward", "sc_conv_uses_tensor_cores", "sc_layer_norm_act", "sc_bf16_round",
     "sc_cast", "sc_subdivide_scratch_bytes", "sc_subdivide",
 )
@@ -64,6 +65,8 @@ class ScEpilogue(ctypes.Structure):
         ("d_out2", ctypes.c_void_p),
         ("d_out_row_map", ctypes.c_void_p),
         ("out_row_map_cols", ctypes.c_int32),
+        ("d_row_order", ctypes.c_void_p),
+        ("d_neighbor_rows_ordered", ctypes.c_void_p),
     ]
 
 
@@ -81,6 +84,8 @@ _SIGS = {
     "sc_neighbor_map": ([_P, _P, _I64, _P, ctypes.c_size_t, _P, _P], ctypes.c_int),
     "sc_neighbor_map_query": ([_P, _P, _I64, _P, _I64, _P, ctypes.c_size_t, _P, _P], ctypes.c_int),
     "sc_neighbor_status": ([_P, ctypes.POINTER(ctypes.c_int32), _P], ctypes.c_int),
+    "sc_neighbor_schedule_scratch_bytes": ([_I64, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "sc_neighbor_schedule": ([_P, _P, _I64, _P, ctypes.c_size_t, _P, _P, _P], ctypes.c_int),
     "sc_subm_conv_forward": ([_P, ctypes.c_int, _P, _I64, _P, _I64, _P, _P, _P, _P, _P], ctypes.c_int),
     "sc_conv_uses_tensor_cores": ([_P, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "sc_layer_norm_act": ([ctypes.c_int, _P, _I64, _I64, _P, _P, ctypes.c_float, ctypes.c_int32,

@@ -65,8 +65,10 @@ class ResBlockStack:
     def conv_count(self) -> int:
         return 2 * len(self.blocks)
 
-    def forward(self, x: torch.Tensor, nbr: torch.Tensor, bufs: dict | None = None) -> torch.Tensor:
-        """x [N, C] (bf16 or f32) -> [N, C]; ``nbr`` is the [N, 27] map."""
+    def forward(self, x: torch.Tensor, nbr: torch.Tensor, bufs: dict | None = None,
+                schedule: "F.ConvSchedule | None" = None) -> torch.Tensor:
+        """x [N, C] (bf16 or f32) -> [N, C]; ``nbr`` is the [N, 27] map;
+        ``schedule`` (optional) its conv schedule (F.neighbor_schedule)."""
         n, c = x.shape
         if bufs is None:
             bufs = {}
@@ -83,15 +85,16 @@ class ResBlockStack:
         for i, p in enumerate(self.blocks):
             h1 = F.sparse_subm_conv_forward(
                 self.cfg, h, nbr, p.w1, p.b1,
-                F.Epilogue(layer_norm=True, ln_eps=p.eps, ln_gamma=p.ln2_g, ln_beta=p.ln2_b, silu=True),
+                F.Epilogue(layer_norm=True, ln_eps=p.eps, ln_gamma=p.ln2_g, ln_beta=p.ln2_b, silu=True,
+                           schedule=schedule),
                 out=buf("h1"))
             nxt = ping[i % 2]
             if i + 1 < len(self.blocks):
                 q = self.blocks[i + 1]
                 e = F.Epilogue(residual=cur, layer_norm=True, ln_eps=q.eps, ln_gamma=q.ln1_g, ln_beta=q.ln1_b,
-                               silu=True, out2=h)
+                               silu=True, out2=h, schedule=schedule)
             else:
-                e = F.Epilogue(residual=cur)
+                e = F.Epilogue(residual=cur, schedule=schedule)
             F.sparse_subm_conv_forward(self.cfg, h1, nbr, p.w2, p.b2, e, out=nxt)
             cur = nxt
         return cur

@@ -23,6 +23,7 @@ struct EpiParams {
     void* out;
     const int32_t* row_map;
     int map_cols;
+    const int32_t* row_order;  // nullable: tile position -> output row
 };
 
 template <typename T>
@@ -62,6 +63,13 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(
         if (tid < SIMT_BM) {
             int64_t r = row0 + tid;
             int32_t v = -1;
+            if (r < n_rows && epi.row_order) {
+                r = epi.row_order[r];
+                if (r < 0 || r >= n_rows) {
+                    raise_fault(FAULT_BAD_NEIGHBOR);
+                    r = n_rows;
+                }
+            }
             if (r < n_rows) {
                 v = __ldg(nbr + r * K + k);
                 if (v < -1 || v >= n_in) {
@@ -123,6 +131,10 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(
     for (int i = 0; i < 4; ++i) {
         int64_t r = row0 + ty * 4 + i;
         if (r >= n_rows) continue;
+        if (epi.row_order) {
+            r = epi.row_order[r];
+            if (r < 0 || r >= n_rows) continue;
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             int oc = col0 + tx * 4 + j;
@@ -142,11 +154,10 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(
     }
 }
 
-// Row-wise LayerNorm (+affine) and/or SiLU over `width`-column groups.
-// Entry e addresses row map[e] (or e when map is null) of x/y, column block
-// (e % blocks_per_entry)...  Simplified: each entry is one row of `width`
-// values at element offset row*ld + col0.  Two-pass statistics as the
-// reference (sparse_decoder_wgpu_ops.rs:1642-1711): mean, then biased
+// Row-wise LayerNorm (+affine) and/or SiLU, one warp per entry.  Entry e is
+// the `width` values at element offset row*ld with row = map[e] (or e when
+// map is null; skipped when negative).  Two-pass statistics as the reference
+// (burn_trellis sparse_decoder_wgpu_ops.rs:1642-1711): mean, then biased
 // variance sum((x-mean)^2)/C, inv_std = 1/sqrt(var + eps).
 template <typename T>
 __global__ void __launch_bounds__(256) rows_norm_act_kernel(

@@ -5,22 +5,29 @@
 // Math (reference: burn_flex_gmm src/lib.rs:242-375 and the device kernels
 // src/wgpu/sparse_conv_kernels.rs:4-46):
 //     out[r, o] = bias[o] + sum_k sum_c in[nbr[r,k], c] * W[o, k, c]
-// computed as a GEMM with M = output rows (tile of 128), N = output channels
-// (tile of up to 512), and the reduction running over (tap k, 64-channel
-// chunk) steps:
-//   * A (128 x 64 bf16 per step) is GATHERED: each of the 128 rows of the
-//     tile copies the 128-byte channel slice of its neighbor row nbr[r,k]
-//     with 16-byte cp.async into a 128B-swizzled K-major smem tile (zero fill
-//     for invalid neighbors or channels >= Cin);
-//   * B (tile_n x 64 bf16 per step) is the weight slice W[n0:n0+tile_n, k,
-//     c0:c0+64], loaded by TMA straight from the reference layout
-//     [Cout, 27, Cin] through a 3-D tensor map (128B swizzle, OOB zero fill);
+// computed as a GEMM with M = output rows (tiles of 128), N = output channels
+// (tiles of up to 512) and the reduction over (tap k, 64-channel chunk) steps:
+//   * A (128 x 64 bf16 per step) is GATHERED from the neighbor rows nbr[r,k]
+//     with 16-byte cp.async into a 128B-swizzled K-major smem tile; every copy
+//     instruction moves whole 128-byte row slices (zero fill for invalid
+//     neighbors and for channels >= Cin);
+//   * B (tile_n x 64 bf16 per step) is W[n0:n0+tile_n, k, c0:c0+64], loaded by
+//     TMA from the reference layout [Cout, 27, Cin] (3-D tensor map, 128B
+//     swizzle, OOB zero fill);
 //   * tcgen05.mma (M=128, N<=256 per instruction, K=16) accumulates in fp32
-//     TMEM; taps with no valid neighbor anywhere in the tile are skipped.
-// Roles (192 threads): warps 0-3 gather A and then run the epilogue (thread i
-// owns TMEM lane / tile row i), warp 4 issues the weight TMA, warp 5 issues
-// the MMAs.  Stage hand-off uses mbarriers; every wait is bounded and raises
-// the device fault word instead of hanging.
+//     TMEM; taps that are invalid for every row of a tile are skipped.
+//
+// Persistent, warp-specialised CTA (one per SM, static round-robin tiles):
+//   warps 0-3          epilogue: thread i owns TMEM lane / tile row i; output
+//                      and residual rows move through padded smem staging so
+//                      that global accesses are whole coalesced rows;
+//   warps 4..4+PW-1    A gather producers; warp 4 lane 0 also issues the
+//                      weight TMA and tags each stage first/last of its tile;
+//   warp 4+PW          MMA issuer (one thread).
+// The accumulator is double-buffered in TMEM (2 x 256 columns) when
+// tile_n <= 256, so the epilogue of one tile overlaps the MMAs of the next.
+// Every mbarrier wait is bounded: on expiry the device fault word is raised
+// and the CTA drains and exits instead of hanging.
 #pragma once
 
 #include "sc_common.cuh"
@@ -30,8 +37,11 @@ namespace sc {
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;                      // channels per reduction step
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
-constexpr int TC_THREADS = 192;
+constexpr int TC_PW = 2;                       // gather producer warps
+constexpr int TC_THREADS = (4 + TC_PW + 1) * 32;
 constexpr int TC_MAX_K = 32;
+constexpr int TC_STG_COLS = 128;               // epilogue staging width (columns)
+constexpr uint32_t TC_TMEM_COLS = 512;
 
 struct TcParams {
     const __nv_bfloat16* in;
@@ -42,11 +52,14 @@ struct TcParams {
     int K;
     const float* bias;
     int cout;
-    int tile_n;   // output columns per CTA (multiple of 32, <= 512)
+    int tile_n;   // output columns per tile (multiple of 32, <= 512)
     int n_sub;    // MMAs per reduction step (1 or 2)
     int sub_n;    // N of each MMA (= TMA box rows), tile_n = n_sub * sub_n
     int stages;
-    uint32_t tmem_cols;
+    int n_buf;    // TMEM accumulator buffers (2 when tile_n <= 256)
+    int grid_y;   // column tiles per row tile
+    int64_t n_tiles;
+    int stg_cols; // epilogue staging width: a multiple of 32 dividing tile_n, <= TC_STG_COLS
     // epilogue
     const __nv_bfloat16* residual;
     const int64_t* res_off;
@@ -61,351 +74,495 @@ struct TcParams {
     __nv_bfloat16* out2;
     const int32_t* row_map;
     int map_cols;
+    const int32_t* row_order;    // nullable: tile position -> output row (a permutation)
+    const int32_t* nbr_ordered;  // nullable: nbr rows in tile order (nbr[row_order[p]])
 };
 
-__device__ __forceinline__ void cp_async_wait_dyn(int n) {
-    if (n <= 0)
-        cp_async_wait<0>();
-    else if (n == 1)
-        cp_async_wait<1>();
-    else
-        cp_async_wait<2>();
+// Output row processed at tile position `pos` (< n_rows), or -1 if invalid.
+__device__ __forceinline__ int64_t ordered_row(const int32_t* order, int64_t pos, int64_t n_rows) {
+    if (!order) return pos;
+    const int32_t r = __ldg(order + pos);
+    if (r < 0 || r >= n_rows) {
+        raise_fault(FAULT_BAD_NEIGHBOR);
+        return -1;
+    }
+    return r;
 }
 
-// 32 consecutive bf16 of `src` (16-byte aligned) -> fp32
-__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32]) {
-    const uint4* p = reinterpret_cast<const uint4*>(src);
+__device__ __forceinline__ void cvt_store_bf16x8(uint8_t* dst, const float* v) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint4 u = __ldg(p + q);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    *reinterpret_cast<uint4*>(dst) = u;
+}
+
+__device__ __forceinline__ void load_bf16x8(const uint8_t* src, float* v) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            float2 f = __bfloat1622float2(h[e]);
-            v[q * 8 + 2 * e] = f.x;
-            v[q * 8 + 2 * e + 1] = f.y;
-        }
+    for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
     }
 }
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
-    uint4* p = reinterpret_cast<uint4*>(dst);
+// Epilogue staging of one warp: 32 rows of `units` 16-byte units, padded by
+// one unit per row so that the owning thread's row writes and the warp's
+// row-wide reads are both free of bank conflicts.
+struct Staging {
+    uint8_t* base;
+    int units;
+    __device__ __forceinline__ uint8_t* at(int r, int u) const { return base + (r * (units + 1) + u) * 16; }
+};
+
+// Staged rows -> global rows orow (per lane = row; < 0 skipped), columns
+// [col0, col0 + 8*units) of a row-major matrix with leading dimension ld.
+__device__ __forceinline__ void store_staged_rows(const Staging& st, int64_t orow, __nv_bfloat16* dst,
+                                                  int64_t ld, int col0, int lane) {
+    const int total = 32 * st.units;
+    for (int idx = lane; idx < total; idx += 32) {
+        const int r = idx / st.units, u = idx - r * st.units;
+        const int64_t o = __shfl_sync(0xffffffffu, orow, r);
+        if (o >= 0)
+            *reinterpret_cast<uint4*>(dst + o * ld + col0 + u * 8) = *reinterpret_cast<const uint4*>(st.at(r, u));
+    }
+}
+
+// Global rows rrow (per lane = row; < 0 gives zeros) -> staged rows.
+__device__ __forceinline__ void load_staged_rows(const Staging& st, int64_t rrow, const __nv_bfloat16* src,
+                                                 int64_t ld, int col0, int lane) {
+    const int total = 32 * st.units;
+    for (int idx = lane; idx < total; idx += 32) {
+        const int r = idx / st.units, u = idx - r * st.units;
+        const int64_t o = __shfl_sync(0xffffffffu, rrow, r);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (o >= 0) v = __ldg(reinterpret_cast<const uint4*>(src + o * ld + col0 + u * 8));
+        *reinterpret_cast<uint4*>(st.at(r, u)) = v;
+    }
+}
+
+__device__ __forceinline__ void add_param32(float (&v)[32], const float* p, bool mul) {
+    const float4* q4 = reinterpret_cast<const float4*>(p);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint4 u;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
-        p[q] = u;
+    for (int q = 0; q < 8; ++q) {
+        const float4 b = __ldg(q4 + q);
+        if (mul) {
+            v[4 * q] *= b.x;
+            v[4 * q + 1] *= b.y;
+            v[4 * q + 2] *= b.z;
+            v[4 * q + 3] *= b.w;
+        } else {
+            v[4 * q] += b.x;
+            v[4 * q + 1] += b.y;
+            v[4 * q + 2] += b.z;
+            v[4 * q + 3] += b.w;
+        }
     }
 }
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-byte alignment for the 128B-swizzle atoms
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int S = p.stages;
+    const int K = p.K;
     const int B_BYTES = p.tile_n * 128;
+    const int stg_cols = p.stg_cols;
+    const int stg_units = stg_cols / 8;
     uint8_t* a_smem = smem;
-    uint8_t* b_smem = smem + S * TC_A_BYTES;
-    int32_t* nbr_s = reinterpret_cast<int32_t*>(b_smem + S * B_BYTES);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(nbr_s + TC_BM * p.K);
+    uint8_t* b_smem = a_smem + S * TC_A_BYTES;
+    uint8_t* stg_smem = b_smem + S * B_BYTES;                                    // 4 warps
+    int32_t* nbr_s = reinterpret_cast<int32_t*>(stg_smem + 4 * 32 * (stg_units + 1) * 16);  // [TC_BM][K]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(nbr_s + TC_BM * K);
     uint64_t* full = bars;
     uint64_t* empty = bars + S;
-    uint64_t* accum_full = bars + 2 * S;
-    uint32_t* misc = reinterpret_cast<uint32_t*>(accum_full + 1);  // [0]=tmem, [1]=tap mask, [2]=abort
+    uint64_t* tmem_full = bars + 2 * S;   // [2]
+    uint64_t* tmem_empty = bars + 2 * S + 2;
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);  // [S]
+    uint32_t* misc = stage_flags + S;     // [0] tmem base, [1] abort
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int64_t tile_base = (int64_t)blockIdx.x * TC_BM;
-    const int n0 = blockIdx.y * p.tile_n;
-    const int K = p.K;
+    const int64_t my_tiles = p.n_tiles > (int64_t)blockIdx.x ? (p.n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int n_chunks = (p.cin + TC_BK - 1) / TC_BK;
+    constexpr int MMA_WARP = 4 + TC_PW;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 128 + 1);  // 128 gathering threads + the TMA arrive
-            mbar_init(&empty[s], 1);       // one tcgen05.commit
+            mbar_init(&full[s], TC_PW * 32 + 1);  // gather lanes (async) + the TMA/flags arrive
+            mbar_init(&empty[s], 1);              // one tcgen05.commit
         }
-        mbar_init(accum_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tmem_full[b], 1);          // tcgen05.commit after a tile's last MMA
+            mbar_init(&tmem_empty[b], 4);         // one arrive per epilogue warp
+        }
         misc[1] = 0;
-        misc[2] = 0;
         fence_mbar_init();
         fence_proxy_async_smem();
     }
-    if (warp == 5) {
-        tmem_alloc(&misc[0], p.tmem_cols);
+    if (warp == MMA_WARP) {
+        tmem_alloc(&misc[0], TC_TMEM_COLS);
         tmem_relinquish();
     }
     if (warp == 4 && lane == 0) tma_prefetch_desc(&wmap);
-
-    // neighbor tile -> smem (contiguous block of the [N, K] map), tap mask
-    __syncthreads();
-    {
-        uint32_t mask = 0;
-        const int64_t g0 = tile_base * K;
-        const int64_t g_end = p.n_rows * K;
-        for (int i = tid; i < TC_BM * K; i += TC_THREADS) {
-            int32_t v = -1;
-            if (g0 + i < g_end) {
-                v = __ldg(p.nbr + g0 + i);
-                if (v < -1 || v >= p.n_in) {
-                    raise_fault(FAULT_BAD_NEIGHBOR);
-                    v = -1;
-                }
-            }
-            nbr_s[i] = v;
-            if (v >= 0) mask |= 1u << (i % K);
-        }
-        if (mask) atomicOr(&misc[1], mask);
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-
     const uint32_t tmem_base = misc[0];
-    const uint32_t tap_mask = misc[1];
-    const int n_chunks = (p.cin + TC_BK - 1) / TC_BK;
-    const int n_iters = __popc(tap_mask) * n_chunks;
+    volatile uint32_t* abort_flag = &misc[1];
 
-    if (warp < 4) {
-        // ------------------------------------------------ A gather producer
-        const int t = tid;  // tile row
-        const int LAG = S > 2 ? 2 : 1;
+    if (warp >= 4 && warp < 4 + TC_PW) {
+        // ====================================================== A producers
+        const int pw = warp - 4;
+        const int sub = lane >> 3;  // row within a group of 4
+        const int j = lane & 7;     // 16-byte chunk of the 128-byte slice
+        constexpr int ROWS = TC_BM / TC_PW;     // rows per producer warp
+        constexpr int GROUPS = ROWS / 4;        // copy instructions per stage
+        int32_t* my_nbr = nbr_s + pw * ROWS * K;
         int it = 0;
         bool ok = true;
-        for (uint32_t m = tap_mask; m && ok; m &= m - 1) {
-            const int k = __ffs(m) - 1;
-            const int32_t src = nbr_s[t * K + k];
-            const __nv_bfloat16* src_row = p.in + (int64_t)(src < 0 ? 0 : src) * p.cin;
-            for (int ch = 0; ch < n_chunks; ++ch) {
-                const int s = it % S;
-                const uint32_t ph = (uint32_t)(it / S) & 1u;
-                if (!mbar_wait(&empty[s], ph ^ 1u)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t dst = smem_u32(a_smem + s * TC_A_BYTES + t * 128);
+        for (int64_t lt = 0; lt < my_tiles && ok; ++lt) {
+            const int64_t tile = blockIdx.x + lt * gridDim.x;
+            const int64_t tile_base = (tile / p.grid_y) * TC_BM;
+            const int n0 = (int)(tile % p.grid_y) * p.tile_n;
+            // neighbor rows of the whole tile (for the common tap mask), mine kept in smem
+            uint32_t mask = 0;
+            const int64_t n_valid = p.n_rows - tile_base < TC_BM ? p.n_rows - tile_base : TC_BM;
+            const int n_ints = (int)n_valid * K;
+            if (p.row_order == nullptr || p.nbr_ordered != nullptr) {
+                // the tile's map rows are contiguous: independent 16-byte loads
+                const int32_t* blk = (p.nbr_ordered ? p.nbr_ordered : p.nbr) + tile_base * K;
+                const int n_vec = (n_ints + 3) / 4;
+                for (int f4 = lane; f4 < n_vec; f4 += 32) {
+                    int4 q;
+                    if (4 * f4 + 3 < n_ints) {
+                        q = __ldg(reinterpret_cast<const int4*>(blk) + f4);
+                    } else {
+                        q.x = 4 * f4 < n_ints ? __ldg(blk + 4 * f4) : -1;
+                        q.y = 4 * f4 + 1 < n_ints ? __ldg(blk + 4 * f4 + 1) : -1;
+                        q.z = 4 * f4 + 2 < n_ints ? __ldg(blk + 4 * f4 + 2) : -1;
+                        q.w = -1;
+                    }
+                    const int32_t vals[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int c = ch * TC_BK + j * 8;
-                    const bool v = src >= 0 && c < p.cin;
-                    cp_async_16(dst + ((j ^ (t & 7)) << 4), v ? (const void*)(src_row + c) : (const void*)p.in,
-                                v ? 16u : 0u);
+                    for (int e = 0; e < 4; ++e) {
+                        const int f = 4 * f4 + e;
+                        if (f >= n_ints) break;
+                        const int t = f / K, k = f - t * K;
+                        int32_t v = vals[e];
+                        if (v < -1 || v >= p.n_in) {
+                            raise_fault(FAULT_BAD_NEIGHBOR);
+                            v = -1;
+                        }
+                        if (v >= 0) mask |= 1u << k;
+                        if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = v;
+                    }
                 }
-                cp_async_commit();
-                if (it >= LAG) {
-                    cp_async_wait_dyn(LAG);
-                    fence_proxy_async_smem();
-                    mbar_arrive(&full[(it - LAG) % S]);
+                for (int f = n_ints + lane; f < TC_BM * K; f += 32) {
+                    const int t = f / K, k = f - t * K;
+                    if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = -1;
                 }
-                ++it;
+            } else {
+                // row order without a pre-ordered map: gather the rows
+                for (int i = lane; i < TC_BM * K; i += 32) {
+                    const int t = i / K, k = i - t * K;
+                    int32_t v = -1;
+                    if (i < n_ints) {
+                        const int64_t r = ordered_row(p.row_order, tile_base + t, p.n_rows);
+                        if (r >= 0) {
+                            v = __ldg(p.nbr + r * K + k);
+                            if (v < -1 || v >= p.n_in) {
+                                raise_fault(FAULT_BAD_NEIGHBOR);
+                                v = -1;
+                            }
+                        }
+                    }
+                    if (v >= 0) mask |= 1u << k;
+                    if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = v;
+                }
             }
-        }
-        cp_async_wait<0>();
-        fence_proxy_async_smem();
-        if (ok) {
-            for (int j = (it > LAG ? it - LAG : 0); j < it; ++j) mbar_arrive(&full[j % S]);
-        } else {
-            atomicOr(&misc[2], 1u);
-        }
-    } else if (warp == 4) {
-        // ------------------------------------------------ weight TMA producer
-        if (lane == 0) {
-            int it = 0;
-            bool ok = true;
-            for (uint32_t m = tap_mask; m && ok; m &= m - 1) {
+            mask = __reduce_or_sync(0xffffffffu, mask);
+            if (mask == 0) mask = 1;  // a tile with no valid tap still runs one (all-zero) step
+            __syncwarp();
+            const int n_steps = __popc(mask) * n_chunks;
+            int step = 0;
+            for (uint32_t m = mask; m && ok; m &= m - 1) {
                 const int k = __ffs(m) - 1;
-                for (int ch = 0; ch < n_chunks; ++ch) {
+                int32_t src[GROUPS];
+#pragma unroll
+                for (int i = 0; i < GROUPS; ++i) src[i] = my_nbr[(i * 4 + sub) * K + k];
+                for (int ch = 0; ch < n_chunks; ++ch, ++step) {
                     const int s = it % S;
                     const uint32_t ph = (uint32_t)(it / S) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)B_BYTES);
-                    const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
-                    for (int j = 0; j < p.n_sub; ++j)
-                        tma_load_3d(dst + j * p.sub_n * 128, &wmap, &full[s], ch * TC_BK, k,
-                                    n0 + j * p.sub_n);
+                    if (pw == 0 && lane == 0) {
+                        stage_flags[s] = (step == 0 ? 1u : 0u) | (step == n_steps - 1 ? 2u : 0u);
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)B_BYTES);
+                        const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
+                        for (int q = 0; q < p.n_sub; ++q)
+                            tma_load_3d(dst + q * p.sub_n * 128, &wmap, &full[s], ch * TC_BK, k,
+                                        n0 + q * p.sub_n);
+                    }
+                    const int c = ch * TC_BK + j * 8;
+                    const uint32_t stage = smem_u32(a_smem + s * TC_A_BYTES);
+#pragma unroll
+                    for (int i = 0; i < GROUPS; ++i) {
+                        const int r = pw * ROWS + i * 4 + sub;
+                        const bool v = src[i] >= 0 && c < p.cin;
+                        const void* g = v ? (const void*)(p.in + (int64_t)src[i] * p.cin + c) : (const void*)p.in;
+                        cp_async_16(stage + r * 128 + ((j ^ (r & 7)) << 4), g, v ? 16u : 0u);
+                    }
+                    cp_async_arrive_noinc(&full[s]);
                     ++it;
                 }
             }
-            if (!ok) atomicOr(&misc[2], 1u);
         }
-    } else {
-        // ------------------------------------------------ MMA issuer (warp 5)
+        cp_async_wait<0>();
+        if (!ok) *abort_flag = 1u;
+    } else if (warp == MMA_WARP) {
+        // ====================================================== MMA issuer
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_bf16_m128((uint32_t)p.sub_n);
+            int it = 0;
             bool ok = true;
-            for (int it = 0; it < n_iters; ++it) {
-                const int s = it % S;
-                const uint32_t ph = (uint32_t)(it / S) & 1u;
-                if (!mbar_wait(&full[s], ph)) {
+            for (int64_t lt = 0; lt < my_tiles && ok; ++lt) {
+                const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
+                const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
+                if (!mbar_wait(&tmem_empty[b], (use & 1u) ^ 1u)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(a_smem + s * TC_A_BYTES);
-                const uint32_t b0 = smem_u32(b_smem + s * B_BYTES);
-#pragma unroll
-                for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                    const uint64_t ad = umma_desc_sw128(a0 + kk * 32);
-                    for (int j = 0; j < p.n_sub; ++j) {
-                        const uint64_t bd = umma_desc_sw128(b0 + j * p.sub_n * 128 + kk * 32);
-                        umma_bf16(tmem_base + j * p.sub_n, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+                const uint32_t acc = tmem_base + (uint32_t)(b * 256);
+                bool first = true;
+                for (;;) {
+                    const int s = it % S;
+                    const uint32_t ph = (uint32_t)(it / S) & 1u;
+                    if (!mbar_wait(&full[s], ph)) {
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    fence_proxy_async_smem();  // cp.async (generic proxy) data -> tcgen05.mma reads
+                    const uint32_t flags = stage_flags[s];
+                    const uint32_t a0 = smem_u32(a_smem + s * TC_A_BYTES);
+                    const uint32_t b0 = smem_u32(b_smem + s * B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 16; ++kk) {
+                        const uint64_t ad = umma_desc_sw128(a0 + kk * 32);
+                        for (int q = 0; q < p.n_sub; ++q) {
+                            const uint64_t bd = umma_desc_sw128(b0 + q * p.sub_n * 128 + kk * 32);
+                            umma_bf16(acc + q * p.sub_n, ad, bd, idesc, (first && kk == 0) ? 0u : 1u);
+                        }
+                    }
+                    umma_commit(&empty[s]);
+                    ++it;
+                    first = false;
+                    if (flags & 2u) break;
                 }
-                umma_commit(&empty[s]);
+                if (!ok) break;
+                umma_commit(&tmem_full[b]);
             }
-            if (ok && n_iters > 0)
-                umma_commit(accum_full);
-            else
-                mbar_arrive(accum_full);
-            if (!ok) atomicOr(&misc[2], 1u);
+            if (!ok) *abort_flag = 1u;
         }
-    }
-
-    // ---------------------------------------------------- epilogue (warps 0-3)
-    if (warp < 4) {
-        // tcgen05.ld/st are warp-collective (.sync.aligned): the decision to
-        // read TMEM must be uniform across the warp.
-        const bool waited = mbar_wait(accum_full, 0);
-        const bool have_acc = __all_sync(0xffffffffu, waited) && n_iters > 0;
-        tc_fence_after();
-        const int t = tid;
-        const int64_t row = tile_base + t;
-        const bool row_ok = row < p.n_rows;
-        const uint32_t lane_addr = tmem_base + ((uint32_t)(warp * 32) << 16);
+    } else {
+        // ====================================================== epilogue
+        Staging st;
+        st.units = stg_units;
+        st.base = stg_smem + warp * 32 * (stg_units + 1) * 16;
+        const int t = tid;  // TMEM lane == tile row
         const int W = p.ln_width;
-        const bool aborted = *reinterpret_cast<volatile uint32_t*>(&misc[2]) != 0;
-
-        // output addressing
-        int64_t orow = row;
-        int ocol0 = n0;
-        int64_t old = p.cout;
-        if (p.row_map) {
-            const int wb = p.cout / p.map_cols;
-            orow = row_ok ? (int64_t)p.row_map[row * p.map_cols + n0 / wb] : -1;
-            ocol0 = n0 % wb;
-            old = wb;
-        }
-        const bool store = row_ok && orow >= 0 && !aborted;
-        const bool multi_pass = p.ln != 0;
-
-        for (int g0 = 0; g0 < p.tile_n; g0 += W) {
-            float mean = 0.f, rstd = 1.f;
-            // pass 1: y = acc + bias + residual (kept in TMEM for later passes)
-            float sum = 0.f;
-            for (int c = g0; c < g0 + W; c += 32) {
-                float v[32];
-                if (have_acc)
-                    tmem_ld32(lane_addr + c, v);
-                else
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] = 0.f;
-                if (p.bias) {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] += __ldg(p.bias + n0 + c + e);
-                }
-                if (p.residual && row_ok) {
-                    if (p.res_off) {
-                        const int64_t base = p.res_off[row];
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            v[e] += __bfloat162float(p.residual[base + (n0 + c + e) / p.res_rep]);
-                    } else {
-                        float r[32];
-                        load_bf16x32(p.residual + row * (int64_t)p.cout + n0 + c, r);
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) v[e] += r[e];
-                    }
-                }
-                if (multi_pass) {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) sum += v[e];
-                    // without an accumulator, y (bias + residual) is recomputed below
-                    if (have_acc) tmem_st32(lane_addr + c, v);
-                } else {
-                    if (store) {
-                        __nv_bfloat16* o = p.out + orow * old + ocol0 + c;
-                        if (p.out2) {
-                            store_bf16x32(o, v);
-                            float a[32];
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) a[e] = p.silu ? silu_f(v[e]) : v[e];
-                            store_bf16x32(p.out2 + orow * old + ocol0 + c, a);
-                        } else {
-                            if (p.silu) {
-#pragma unroll
-                                for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
-                            }
-                            store_bf16x32(o, v);
-                        }
-                    }
-                }
+        const bool multi = p.ln != 0 || p.out2 != nullptr;
+        const bool dense_res = p.residual != nullptr && p.res_off == nullptr;
+        for (int64_t lt = 0; lt < my_tiles; ++lt) {
+            const int64_t tile = blockIdx.x + lt * gridDim.x;
+            const int64_t tile_base = (tile / p.grid_y) * TC_BM;
+            const int n0 = (int)(tile % p.grid_y) * p.tile_n;
+            const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
+            const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
+            const bool waited = mbar_wait(&tmem_full[b], use & 1u);
+            if (!__all_sync(0xffffffffu, waited)) {
+                *abort_flag = 1u;
+                break;
             }
-            if (!multi_pass) continue;
-            mean = sum / (float)W;
-            // helper to re-materialise y for column block c
-            auto load_y = [&](int c, float (&v)[32]) {
-                if (have_acc) {
-                    tmem_ld32(lane_addr + c, v);
-                } else {
+            tc_fence_after();
+            const uint32_t lane_addr = tmem_base + (uint32_t)(b * 256) + ((uint32_t)(warp * 32) << 16);
+            const int64_t pos = tile_base + t;
+            const int64_t row = pos < p.n_rows ? ordered_row(p.row_order, pos, p.n_rows) : -1;
+            int64_t orow = row, old = p.cout;
+            int ocol0 = n0;
+            if (p.row_map) {
+                const int wb = p.cout / p.map_cols;
+                orow = row >= 0 ? (int64_t)p.row_map[row * p.map_cols + n0 / wb] : -1;
+                ocol0 = n0 % wb;
+                old = wb;
+            }
+
+            // y = acc + bias + residual for the 32 columns at tile column c
+            // (staging group starting at g0 holds the dense residual)
+            auto compute_y = [&](int c, int g0, float (&v)[32]) {
+                tmem_ld32(lane_addr + c, v);
+                if (p.bias) add_param32(v, p.bias + n0 + c, false);
+                if (dense_res) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] = p.bias ? __ldg(p.bias + n0 + c + e) : 0.f;
-                    if (p.residual && row_ok) {
-                        if (p.res_off) {
-                            const int64_t base = p.res_off[row];
+                    for (int q = 0; q < 4; ++q) {
+                        float r8[8];
+                        load_bf16x8(st.at(lane, (c - g0) / 8 + q), r8);
 #pragma unroll
-                            for (int e = 0; e < 32; ++e)
-                                v[e] += __bfloat162float(p.residual[base + (n0 + c + e) / p.res_rep]);
-                        } else {
-                            float r[32];
-                            load_bf16x32(p.residual + row * (int64_t)p.cout + n0 + c, r);
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) v[e] += r[e];
-                        }
+                        for (int e = 0; e < 8; ++e) v[q * 8 + e] += r8[e];
                     }
+                } else if (p.residual && row >= 0) {
+                    const int64_t base = p.res_off[row];
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        v[e] += __bfloat162float(p.residual[base + (n0 + c + e) / p.res_rep]);
                 }
             };
-            // pass 2: biased variance about the mean (two-pass, as the reference)
-            float var = 0.f;
-            for (int c = g0; c < g0 + W; c += 32) {
-                float v[32];
-                load_y(c, v);
+            auto stage_out = [&](int c, int g0, const float (&v)[32]) {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const float d = v[e] - mean;
-                    var += d * d;
+                for (int q = 0; q < 4; ++q) cvt_store_bf16x8(st.at(lane, (c - g0) / 8 + q), v + 8 * q);
+            };
+
+            if (!multi) {
+                for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
+                    if (dense_res) {
+                        load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane);
+                        __syncwarp();
+                    }
+                    for (int c = g0; c < g0 + stg_cols; c += 32) {
+                        float v[32];
+                        compute_y(c, g0, v);
+                        if (p.silu) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
+                        }
+                        stage_out(c, g0, v);
+                    }
+                    __syncwarp();
+                    store_staged_rows(st, orow, p.out, old, ocol0 + g0, lane);
+                    __syncwarp();
+                }
+            } else {
+                // pass 1: y -> TMEM (residual folded in) and per-group sums
+                float sum[4] = {0.f, 0.f, 0.f, 0.f};  // <= 4 LayerNorm groups per tile
+                for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
+                    if (dense_res) {
+                        load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane);
+                        __syncwarp();
+                    }
+                    for (int c = g0; c < g0 + stg_cols; c += 32) {
+                        float v[32];
+                        compute_y(c, g0, v);
+                        float s = 0.f;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) s += v[e];
+                        const int g = c / W;
+                        sum[0] += g == 0 ? s : 0.f;
+                        sum[1] += g == 1 ? s : 0.f;
+                        sum[2] += g == 2 ? s : 0.f;
+                        sum[3] += g == 3 ? s : 0.f;
+                        tmem_st32(lane_addr + c, v);
+                    }
+                    __syncwarp();
+                }
+                float mean[4], rstd[4] = {1.f, 1.f, 1.f, 1.f};
+#pragma unroll
+                for (int g = 0; g < 4; ++g) mean[g] = sum[g] / (float)W;
+                if (p.ln) {
+                    // pass 2: biased variance about the mean (two-pass, as the reference)
+                    float var[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int c = 0; c < p.tile_n; c += 32) {
+                        float v[32];
+                        tmem_ld32(lane_addr + c, v);
+                        const int g = c / W;
+                        const float mu = g == 0 ? mean[0] : g == 1 ? mean[1] : g == 2 ? mean[2] : mean[3];
+                        float s = 0.f;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            const float d = v[e] - mu;
+                            s += d * d;
+                        }
+                        var[0] += g == 0 ? s : 0.f;
+                        var[1] += g == 1 ? s : 0.f;
+                        var[2] += g == 2 ? s : 0.f;
+                        var[3] += g == 3 ? s : 0.f;
+                    }
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) rstd[g] = 1.0f / sqrtf(var[g] / (float)W + p.eps);
+                }
+                // pass 3: out = y when a second output is requested
+                if (p.out2) {
+                    for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
+                        for (int c = g0; c < g0 + stg_cols; c += 32) {
+                            float v[32];
+                            tmem_ld32(lane_addr + c, v);
+                            stage_out(c, g0, v);
+                        }
+                        __syncwarp();
+                        store_staged_rows(st, orow, p.out, old, ocol0 + g0, lane);
+                        __syncwarp();
+                    }
+                }
+                // pass 4: post(y) = [LayerNorm(gamma, beta)] -> [SiLU]
+                __nv_bfloat16* dst = p.out2 ? p.out2 : p.out;
+                for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
+                    for (int c = g0; c < g0 + stg_cols; c += 32) {
+                        float v[32];
+                        tmem_ld32(lane_addr + c, v);
+                        if (p.ln) {
+                            const int g = c / W;
+                            const int gc = c - g * W;
+                            const float mu = g == 0 ? mean[0] : g == 1 ? mean[1] : g == 2 ? mean[2] : mean[3];
+                            const float rs = g == 0 ? rstd[0] : g == 1 ? rstd[1] : g == 2 ? rstd[2] : rstd[3];
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] = (v[e] - mu) * rs;
+                            if (p.gamma) add_param32(v, p.gamma + gc, true);
+                            if (p.beta) add_param32(v, p.beta + gc, false);
+                        }
+                        if (p.silu) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
+                        }
+                        stage_out(c, g0, v);
+                    }
+                    __syncwarp();
+                    store_staged_rows(st, orow, dst, old, ocol0 + g0, lane);
+                    __syncwarp();
                 }
             }
-            rstd = 1.0f / sqrtf(var / (float)W + p.eps);
-            // pass 3: outputs
-            for (int c = g0; c < g0 + W; c += 32) {
-                float v[32];
-                load_y(c, v);
-                if (store && p.out2) store_bf16x32(p.out + orow * old + ocol0 + c, v);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    float a = (v[e] - mean) * rstd;
-                    const int gc = c - g0 + e;
-                    if (p.gamma) a *= __ldg(p.gamma + gc);
-                    if (p.beta) a += __ldg(p.beta + gc);
-                    v[e] = p.silu ? silu_f(a) : a;
-                }
-                if (store) store_bf16x32((p.out2 ? p.out2 : p.out) + orow * old + ocol0 + c, v);
-            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[b]);
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == MMA_WARP) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, p.tmem_cols);
+        tmem_dealloc(tmem_base, TC_TMEM_COLS);
     }
+}
+
+// Epilogue staging width: the largest multiple of 32 that divides tile_n
+// and is at most TC_STG_COLS, so staging groups tile the row exactly.
+inline int tc_stg_cols(int tile_n) {
+    for (int c = TC_STG_COLS; c >= 32; c -= 32)
+        if (tile_n % c == 0) return c;
+    return 32;
+}
+
+// Dynamic shared-memory bytes of a launch (1 KB alignment slack included).
+inline size_t tc_smem_bytes(int stages, int tile_n, int K) {
+    const int stg_cols = tc_stg_cols(tile_n);
+    return 1024 + (size_t)stages * (TC_A_BYTES + (size_t)tile_n * 128) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
+           (size_t)TC_BM * K * 4 + (2 * stages + 4) * 8 + stages * 4 + 16;
 }
 
 }  // namespace sc

@@ -64,4 +64,33 @@ __global__ void subdiv_write_kernel(const int4* __restrict__ parent_coords,
     }
 }
 
+// --- mask-sorted row order ----------------------------------------------------
+// key[r] = sum_j valid(r, tap_rank[j]) << (K-1-j): taps ranked farthest-from-
+// centre first, so rows with equal outer-tap patterns end up adjacent.
+struct TapRank {
+    int32_t k;
+    int8_t rank_of_tap[32];  // bit position (K-1-rank) for each tap
+};
+
+__global__ void row_mask_key_kernel(const int32_t* __restrict__ nbr, int64_t n, const TapRank tr,
+                                    uint32_t* __restrict__ keys, int32_t* __restrict__ vals) {
+    int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n) return;
+    uint32_t key = 0;
+    for (int k = 0; k < tr.k; ++k)
+        if (__ldg(nbr + r * tr.k + k) >= 0) key |= 1u << (tr.k - 1 - tr.rank_of_tap[k]);
+    keys[r] = key;
+    vals[r] = (int32_t)r;
+}
+
+// ordered[p, :] = nbr[order[p], :]
+__global__ void permute_rows_kernel(const int32_t* __restrict__ nbr, const int32_t* __restrict__ order,
+                                    int64_t n, int K, int32_t* __restrict__ ordered) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * K) return;
+    const int64_t p = i / K;
+    const int k = (int)(i - p * K);
+    ordered[i] = __ldg(nbr + (int64_t)__ldg(order + p) * K + k);
+}
+
 }  // namespace sc

@@ -134,6 +134,11 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint3
                  "r"(src_bytes)
                  : "memory");
 }
+// Arrive on `bar` once all prior cp.async of this thread have completed;
+// .noinc: the arrival counts toward the barrier's expected arrival count.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {

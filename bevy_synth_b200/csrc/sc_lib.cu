@@ -5,6 +5,7 @@
 // (burn_flex_gmm src/lib.rs:698-725 validate_config; src/wgpu/sparse_conv.rs:
 // 369-473 validate_tensor_shapes) and reports them as SC_ERR_INVALID with a
 // message, as the reference returns Err(String).
+#include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_scan.cuh>
 
 #include <algorithm>
@@ -99,12 +100,23 @@ static bool force_simt() {
 }
 
 struct TcPlan {
-    int tile_n, n_sub, sub_n, stages, grid_y;
-    uint32_t tmem_cols;
+    int tile_n, n_sub, sub_n, stages, grid_y, n_buf;
     size_t smem;
 };
 
 static constexpr size_t kMaxDynSmem = 232448;  // 227 KB opt-in per block on sm_100
+
+static int sm_count() {
+    static int count[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (count[dev] == 0) {
+        int c = 0;
+        if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+        count[dev] = c;
+    }
+    return count[dev];
+}
 
 // Decides whether the tensor-core kernel takes this conv and with which tiling.
 static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, TcPlan* plan) {
@@ -116,12 +128,9 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
         if (e.out_row_map_cols <= 0 || cout % e.out_row_map_cols != 0) return false;
         tile_n = (int)(cout / e.out_row_map_cols);
         if (e.layer_norm && e.ln_width != 0 && e.ln_width != tile_n) return false;
-    } else if (e.layer_norm) {
-        const int64_t W = e.ln_width ? e.ln_width : cout;
-        if (cout <= 512)
-            tile_n = (int)cout;
-        else
-            tile_n = (int)W;
+    } else if (e.layer_norm || e.d_out2) {
+        const int64_t W = (e.layer_norm && e.ln_width) ? e.ln_width : cout;
+        tile_n = (int)(cout <= 512 ? cout : W);
         if (tile_n % W != 0 || cout % tile_n != 0) return false;
     } else {
         int64_t n_tiles = (cout + 255) / 256;
@@ -129,24 +138,23 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
         tile_n = (int)(cout / n_tiles);
     }
     if (tile_n > 512 || tile_n % 32 != 0) return false;
-    if (e.layer_norm) {
-        const int64_t W = e.ln_width ? e.ln_width : (e.d_out_row_map ? tile_n : cout);
-        if (W % 32 != 0 || tile_n % W != 0) return false;
-    }
+    const int64_t W = (e.layer_norm && e.ln_width) ? e.ln_width : tile_n;
+    if (W % 32 != 0 || tile_n % W != 0 || tile_n / W > 4) return false;
     plan->tile_n = tile_n;
     plan->n_sub = tile_n > 256 ? 2 : 1;
     plan->sub_n = tile_n / plan->n_sub;
     if (plan->sub_n % 16 != 0) return false;
-    uint32_t cols = 32;
-    while (cols < (uint32_t)tile_n) cols <<= 1;
-    plan->tmem_cols = cols;
+    plan->n_buf = tile_n <= 256 ? 2 : 1;
     plan->grid_y = (int)(cout / tile_n);
-    const size_t fixed = 1024 + (size_t)TC_BM * K * 4 + 64 * 8 + 64;
-    const size_t stage = TC_A_BYTES + (size_t)tile_n * 128;
-    int S = (int)std::min<size_t>(6, (kMaxDynSmem - fixed) / stage);
+    int S = 8;
+    while (S >= 2 && tc_smem_bytes(S, tile_n, (int)K) > kMaxDynSmem) --S;
+    if (const char* env = std::getenv("SC_TC_STAGES")) {  // tuning override, clamped to what fits
+        const int want = std::atoi(env);
+        if (want >= 2 && want < S) S = want;
+    }
     if (S < 2) return false;
     plan->stages = S;
-    plan->smem = fixed + S * stage;
+    plan->smem = tc_smem_bytes(S, tile_n, (int)K);
     return true;
 }
 
@@ -181,7 +189,12 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     p.n_sub = plan.n_sub;
     p.sub_n = plan.sub_n;
     p.stages = plan.stages;
-    p.tmem_cols = plan.tmem_cols;
+    p.n_buf = plan.n_buf;
+    p.grid_y = plan.grid_y;
+    p.n_tiles = ((n_rows + TC_BM - 1) / TC_BM) * plan.grid_y;
+    p.stg_cols = tc_stg_cols(plan.tile_n);
+    if (p.stg_cols % 32 != 0 || plan.tile_n % p.stg_cols != 0)
+        return fail(SC_ERR_UNSUPPORTED, "internal: staging width does not tile the output tile");
     p.residual = static_cast<const __nv_bfloat16*>(e.d_residual);
     p.res_off = e.d_residual_offset;
     p.res_rep = e.residual_repeat > 0 ? e.residual_repeat : 1;
@@ -195,6 +208,8 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     p.out2 = static_cast<__nv_bfloat16*>(e.d_out2);
     p.row_map = e.d_out_row_map;
     p.map_cols = e.d_out_row_map ? e.out_row_map_cols : 1;
+    p.row_order = e.d_row_order;
+    p.nbr_ordered = e.d_row_order ? e.d_neighbor_rows_ordered : nullptr;
 
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
@@ -203,8 +218,8 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
                                         (int)kMaxDynSmem);
     });
     SC_CUDA_TRY(attr_err);
-    dim3 grid((unsigned)((n_rows + TC_BM - 1) / TC_BM), (unsigned)plan.grid_y);
-    conv_tc_kernel<<<grid, TC_THREADS, plan.smem, st>>>(wmap, p);
+    const int64_t ctas = std::min<int64_t>(p.n_tiles, sm_count());
+    conv_tc_kernel<<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, p);
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
 }
@@ -223,6 +238,7 @@ static int launch_simt(const sc_conv_config* c, const void* in, int64_t n_in, co
     ep.out = out;
     ep.row_map = e.d_out_row_map;
     ep.map_cols = e.d_out_row_map ? e.out_row_map_cols : 1;
+    ep.row_order = e.d_row_order;
     dim3 grid(grid1d(n_rows, SIMT_BM), (unsigned)(bpg * c->groups));
     conv_simt_kernel<T><<<grid, 256, 0, st>>>(
         static_cast<const T*>(in), n_in, (int)c->in_channels, (int)c->in_channels_per_group, nbr,
@@ -360,6 +376,62 @@ int sc_neighbor_status(const void* ws, int32_t* h_max_probe, void* stream) {
     if (h.bits & NB_STATUS_RANGE)
         return fail(SC_ERR_RANGE, "sparse conv coordinate component outside [0, 65534]");
     if (h.bits & NB_STATUS_CAPACITY) return fail(SC_ERR_CAPACITY, "neighbor hash table insert failed");
+    return SC_OK;
+}
+
+static size_t order_cub_bytes(int64_t n) {
+    size_t b = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, b, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                    (const int32_t*)nullptr, (int32_t*)nullptr, (int)n, 0, 32);
+    return b;
+}
+
+static size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+int sc_neighbor_schedule_scratch_bytes(int64_t n, size_t* bytes) {
+    if (n < 0 || !bytes) return fail(SC_ERR_INVALID, "invalid row order scratch query");
+    *bytes = 3 * align256((size_t)n * 4) + order_cub_bytes(n) + 256;
+    return SC_OK;
+}
+
+int sc_neighbor_schedule(const sc_conv_config* cfg, const int32_t* nbr, int64_t n, void* scratch,
+                         size_t scratch_bytes, int32_t* order, int32_t* nbr_ordered, void* stream) {
+    if (int rc = validate_config(cfg)) return rc;
+    const int64_t K = kernel_rows_of(cfg);
+    if (K > 32) return fail(SC_ERR_UNSUPPORTED, "row order supports at most 32 kernel offsets");
+    if (n < 0) return fail(SC_ERR_INVALID, "negative row count");
+    if (n == 0) return SC_OK;
+    if (n > 0x7fffffffLL) return fail(SC_ERR_UNSUPPORTED, "too many rows");
+    size_t need = 0;
+    sc_neighbor_schedule_scratch_bytes(n, &need);
+    if (!scratch || scratch_bytes < need)
+        return fail(SC_ERR_CAPACITY, "row order scratch too small: need " + std::to_string(need) + " bytes");
+    if (!nbr || !order) return fail(SC_ERR_INVALID, "null pointer");
+    // rank taps by L1 distance from the centre, farthest first (ties by index)
+    int32_t off[3 * 32];
+    kernel_offsets_of(cfg, off);
+    TapRank tr;
+    tr.k = (int32_t)K;
+    int idx[32];
+    for (int i = 0; i < K; ++i) idx[i] = i;
+    auto l1 = [&](int i) { return std::abs(off[3 * i]) + std::abs(off[3 * i + 1]) + std::abs(off[3 * i + 2]); };
+    std::stable_sort(idx, idx + K, [&](int a, int b) { return l1(a) > l1(b); });
+    for (int r = 0; r < K; ++r) tr.rank_of_tap[idx[r]] = (int8_t)r;
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    uint32_t* keys_in = reinterpret_cast<uint32_t*>(base);
+    uint32_t* keys_out = reinterpret_cast<uint32_t*>(base + align256((size_t)n * 4));
+    int32_t* vals_in = reinterpret_cast<int32_t*>(base + 2 * align256((size_t)n * 4));
+    void* tmp = base + 3 * align256((size_t)n * 4);
+    size_t tmp_bytes = order_cub_bytes(n);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    row_mask_key_kernel<<<grid1d(n, 256), 256, 0, st>>>(nbr, n, tr, keys_in, vals_in);
+    SC_CUDA_TRY(cudaGetLastError());
+    SC_CUDA_TRY(cub::DeviceRadixSort::SortPairs(tmp, tmp_bytes, keys_in, keys_out, vals_in, order, (int)n, 0,
+                                                (int)K, st));
+    if (nbr_ordered) {
+        permute_rows_kernel<<<grid1d(n * K, 256), 256, 0, st>>>(nbr, order, n, (int)K, nbr_ordered);
+        SC_CUDA_TRY(cudaGetLastError());
+    }
     return SC_OK;
 }
 

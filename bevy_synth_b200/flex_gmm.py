@@ -150,6 +150,30 @@ def neighbor_rows_tensor_from_coords_tensor(config: SparseSubmConvConfig, coords
 
 
 @dataclass
+class ConvSchedule:
+    """Row order of a neighbor map (rows grouped by equal valid-tap masks so
+    tensor-core tiles skip more taps) and the map permuted into that order.
+    Computed once per map; changes scheduling only, never results."""
+
+    order: torch.Tensor          # [N] int32 permutation: tile position -> output row
+    nbr_ordered: torch.Tensor    # [N, K] int32 = nbr[order]
+
+
+def neighbor_schedule(config: SparseSubmConvConfig, neighbor_rows: torch.Tensor) -> ConvSchedule:
+    _require_cuda("neighbor_rows", neighbor_rows)
+    n = neighbor_rows.shape[0]
+    b = ctypes.c_size_t(0)
+    check(lib().sc_neighbor_schedule_scratch_bytes(n, ctypes.byref(b)))
+    scratch = torch.empty(max(b.value, 1), dtype=torch.uint8, device=neighbor_rows.device)
+    order = torch.empty(n, dtype=torch.int32, device=neighbor_rows.device)
+    ordered = torch.empty_like(neighbor_rows)
+    c = config.c()
+    check(lib().sc_neighbor_schedule(ctypes.byref(c), _ptr(neighbor_rows), n, _ptr(scratch), b.value, _ptr(order),
+                                     _ptr(ordered), _stream(neighbor_rows)))
+    return ConvSchedule(order, ordered)
+
+
+@dataclass
 class Epilogue:
     """Fused conv epilogue (see sc_epilogue in include/sparseconv.h).
 
@@ -168,13 +192,19 @@ class Epilogue:
     out2: torch.Tensor | None = None
     out_row_map: torch.Tensor | None = None
     out_row_map_cols: int = 0
+    row_order: torch.Tensor | None = None
+    nbr_ordered: torch.Tensor | None = None
+    schedule: ConvSchedule | None = None
     _keep: list = field(default_factory=list, repr=False)
 
     def c(self) -> ScEpilogue:
+        order, ordered = self.row_order, self.nbr_ordered
+        if self.schedule is not None:
+            order, ordered = self.schedule.order, self.schedule.nbr_ordered
         return ScEpilogue(_ptr(self.residual), _ptr(self.residual_offset), int(self.residual_repeat),
                           int(self.layer_norm), int(self.ln_width), float(self.ln_eps), _ptr(self.ln_gamma),
                           _ptr(self.ln_beta), int(self.silu), _ptr(self.out2), _ptr(self.out_row_map),
-                          int(self.out_row_map_cols))
+                          int(self.out_row_map_cols), _ptr(order), _ptr(ordered))
 
 
 _DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16}

@@ -91,6 +91,13 @@ typedef struct sc_epilogue {
                                       to output row d_out_row_map[i*cols + b] (skip if < 0);
                                       the output then has row width Cout / cols */
     int32_t out_row_map_cols;
+    const int32_t* d_row_order;    /* nullable [n_rows] permutation: the order in which output
+                                      rows are grouped into tiles (sc_neighbor_schedule);
+                                      changes scheduling only, never results */
+    const int32_t* d_neighbor_rows_ordered; /* nullable [n_rows, K]: d_neighbor_rows permuted into
+                                      tile order (row p = row d_row_order[p]), as written by
+                                      sc_neighbor_schedule; lets tiles read their map rows
+                                      contiguously */
 } sc_epilogue;
 
 /* ---- library / errors -------------------------------------------------- */
@@ -123,6 +130,18 @@ int sc_neighbor_map_query(const sc_conv_config* cfg, const int32_t* d_in_coords,
  * last map built in this workspace (SC_ERR_RANGE / SC_ERR_CAPACITY).
  * h_max_probe (nullable) receives the longest insert probe sequence. */
 int sc_neighbor_status(const void* d_workspace, int32_t* h_max_probe, void* stream);
+
+/* Conv schedule of a neighbor map, computed once and reused by every conv on
+ * the same map: a processing order of output rows that groups rows with equal
+ * neighbor masks (valid-tap bit patterns) so that tensor-core tiles skip more
+ * taps, and (optional, nullable) the map permuted into that order.  Rows are
+ * sorted by a K-bit key whose most significant bits are the taps farthest
+ * from the centre; the sort is stable, so Morton order is kept within a
+ * group.  K <= 32. */
+int sc_neighbor_schedule_scratch_bytes(int64_t n_rows, size_t* h_bytes);
+int sc_neighbor_schedule(const sc_conv_config* cfg, const int32_t* d_neighbor_rows, int64_t n_rows,
+                         void* d_scratch, size_t scratch_bytes, int32_t* d_row_order,
+                         int32_t* d_neighbor_rows_ordered, void* stream);
 
 /* ---- convolution ----------------------------------------------------------
  * out[n_rows, Cout] = bias + sum_k sum_c in[nbr[r,k], c] * W[o,k,c]  (+ epilogue)

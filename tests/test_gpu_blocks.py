@@ -88,3 +88,19 @@ def test_full_size_config2_stack_tc_vs_fp32(cuda_device, monkeypatch):
     r = float(torch.linalg.norm(y_bf - y_32) / torch.linalg.norm(y_32))
     assert r <= 1e-2, r
     assert_no_fault()
+
+
+def test_resblock_stack_with_schedule_matches_plain(cuda_device):
+    coords = shell()
+    rng = np.random.default_rng(3)
+    c = 128
+    x = rng.standard_normal((coords.shape[0], c)).astype(np.float32)
+    params = [synth.resblock_params(rng, c) for _ in range(2)]
+    cfg = F.SparseSubmConvConfig.subm3(c, c)
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords))
+    stack = blocks.ResBlockStack([blocks.ResBlockParams.from_numpy(p, dev()) for p in params])
+    xt = to_dev(x, torch.bfloat16)
+    a = stack.forward(xt, nbr).float().clone()
+    b = stack.forward(xt, nbr, schedule=F.neighbor_schedule(cfg, nbr)).float()
+    assert rel_l2(b.cpu().numpy(), a.cpu().numpy()) <= 1e-6
+    assert_no_fault()

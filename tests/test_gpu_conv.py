@@ -254,3 +254,63 @@ def test_full_size_config2_layer_sampled_rows(cuda_device):
                                 nb[rows], threads=8)
     assert rel_l2(out[rows], exp) <= 4e-3
     assert_no_fault()
+
+
+def test_schedule_is_a_permutation_and_changes_nothing(cuda_device):
+    wl = synth.config1(0)
+    coords = wl.coords
+    cfg = F.SparseSubmConvConfig.subm3(64, 64)
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords))
+    sched = F.neighbor_schedule(cfg, nbr)
+    order = sched.order
+    o = order.cpu().numpy()
+    np.testing.assert_array_equal(sched.nbr_ordered.cpu().numpy(), nbr.cpu().numpy()[o])
+    assert np.array_equal(np.sort(o), np.arange(coords.shape[0]))
+    # keys are non-decreasing along the order (stable radix sort)
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((coords.shape[0], 64)).astype(np.float32)
+    w = (rng.standard_normal((64, 3, 3, 3, 64)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(64).astype(np.float32)
+    base, _ = conv_gpu(cfg, coords, x, w, b, BF16, nbr=nbr)
+    ordered, _ = conv_gpu(cfg, coords, x, w, b, BF16, F.Epilogue(schedule=sched), nbr=nbr)
+    assert rel_l2(ordered, base) <= 1e-6
+    gathered, _ = conv_gpu(cfg, coords, x, w, b, BF16, F.Epilogue(row_order=order), nbr=nbr)
+    assert rel_l2(gathered, base) <= 1e-6
+    f32, _ = conv_gpu(cfg, coords, x, w, b, torch.float32, F.Epilogue(row_order=order), nbr=nbr)
+    exp = oracle.subm_conv_flex(ocfg(cfg), w, b, x, nbr.cpu().numpy(), threads=8)
+    assert rel_l2(f32, exp) <= 1e-4
+    assert_no_fault()
+
+
+@pytest.mark.parametrize("c", [96, 192, 320, 384])
+def test_bf16_epilogue_writes_stay_inside_rows(cuda_device, c):
+    """Outputs go to a view in the middle of a sentinel-filled buffer: the
+    guard rows before and after must be untouched, and every element of the
+    view must match the oracle (widths whose staging groups are not 128)."""
+    coords = shell(grid=20, r=6.0)
+    n = coords.shape[0]
+    rng = np.random.default_rng(c)
+    x = rng.standard_normal((n, c)).astype(np.float32)
+    w = (rng.standard_normal((c, 3, 3, 3, c)) * 0.03).astype(np.float32)
+    b = (0.1 * rng.standard_normal(c)).astype(np.float32)
+    res = rng.standard_normal((n, c)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(c)).astype(np.float32)
+    be = (0.1 * rng.standard_normal(c)).astype(np.float32)
+    cfg = F.SparseSubmConvConfig.subm3(c, c)
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords))
+    big = torch.full((n + 16, c), 7.0, dtype=BF16, device="cuda:0")
+    big2 = torch.full((n + 16, c), 7.0, dtype=BF16, device="cuda:0")
+    out, out2 = big[8:8 + n], big2[8:8 + n]
+    epi = F.Epilogue(residual=to_dev(res, BF16), layer_norm=True, ln_eps=1e-5, ln_gamma=to_dev(g),
+                     ln_beta=to_dev(be), silu=True, out2=out2)
+    F.sparse_subm_conv_forward(cfg, to_dev(x, BF16), nbr, to_dev(w, BF16), to_dev(b), epi, out=out)
+    torch.cuda.synchronize()
+    for t in (big, big2):
+        guard = torch.cat([t[:8], t[8 + n:]]).float()
+        assert torch.all(guard == 7.0), "write outside the output rows"
+    y = bf16_ref(cfg, x, w, b, nbr.cpu().numpy()) + oracle.bf16_round(res)
+    assert rel_l2(out.float().cpu().numpy(), y) <= 1e-2
+    assert rel_l2(out2.float().cpu().numpy(), oracle.silu(oracle.layer_norm(y, g, be, 1e-5))) <= 1e-2
+    plain = F.sparse_subm_conv_forward(cfg, to_dev(x, BF16), nbr, to_dev(w, BF16), to_dev(b))
+    assert rel_l2(plain.float().cpu().numpy(), bf16_ref(cfg, x, w, b, nbr.cpu().numpy())) <= 4e-3
+    assert_no_fault()
