@@ -233,36 +233,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int64_t n_valid = p.n_rows - tile_base < TC_BM ? p.n_rows - tile_base : TC_BM;
             const int n_ints = (int)n_valid * K;
             if (p.row_order == nullptr || p.nbr_ordered != nullptr) {
-                // the tile's map rows are contiguous: independent 16-byte loads
+                // the tile's map rows are contiguous: independent 16-byte loads,
+                // issued 8 deep before any is consumed (one latency per batch)
                 const int32_t* blk = (p.nbr_ordered ? p.nbr_ordered : p.nbr) + tile_base * K;
+                const int n_full = n_ints / 4;               // whole int4 vectors
                 const int n_vec = (n_ints + 3) / 4;
-                for (int f4 = lane; f4 < n_vec; f4 += 32) {
-                    int4 q;
-                    if (4 * f4 + 3 < n_ints) {
-                        q = __ldg(reinterpret_cast<const int4*>(blk) + f4);
-                    } else {
-                        q.x = 4 * f4 < n_ints ? __ldg(blk + 4 * f4) : -1;
-                        q.y = 4 * f4 + 1 < n_ints ? __ldg(blk + 4 * f4 + 1) : -1;
-                        q.z = 4 * f4 + 2 < n_ints ? __ldg(blk + 4 * f4 + 2) : -1;
-                        q.w = -1;
-                    }
-                    const int32_t vals[4] = {q.x, q.y, q.z, q.w};
+                const uint32_t kdiv = (1u << 20) / (uint32_t)K + 1u;  // f / K == (f * kdiv) >> 20 here
+                for (int base = 0; base < n_vec; base += 8 * 32) {
+                    int4 q[8];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int f = 4 * f4 + e;
-                        if (f >= n_ints) break;
-                        const int t = f / K, k = f - t * K;
-                        int32_t v = vals[e];
-                        if (v < -1 || v >= p.n_in) {
-                            raise_fault(FAULT_BAD_NEIGHBOR);
-                            v = -1;
+                    for (int u = 0; u < 8; ++u) {
+                        const int f4 = base + u * 32 + lane;
+                        if (f4 < n_full) {
+                            q[u] = __ldg(reinterpret_cast<const int4*>(blk) + f4);
+                        } else {
+                            q[u].x = 4 * f4 < n_ints ? __ldg(blk + 4 * f4) : -1;
+                            q[u].y = 4 * f4 + 1 < n_ints ? __ldg(blk + 4 * f4 + 1) : -1;
+                            q[u].z = 4 * f4 + 2 < n_ints ? __ldg(blk + 4 * f4 + 2) : -1;
+                            q[u].w = -1;
                         }
-                        if (v >= 0) mask |= 1u << k;
-                        if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = v;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int f4 = base + u * 32 + lane;
+                        const int32_t vals[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int f = 4 * f4 + e;
+                            if (f >= n_ints) break;
+                            const int t = (int)(((uint32_t)f * kdiv) >> 20), k = f - t * K;
+                            int32_t v = vals[e];
+                            if (v < -1 || v >= p.n_in) {
+                                raise_fault(FAULT_BAD_NEIGHBOR);
+                                v = -1;
+                            }
+                            if (v >= 0) mask |= 1u << k;
+                            if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = v;
+                        }
                     }
                 }
                 for (int f = n_ints + lane; f < TC_BM * K; f += 32) {
-                    const int t = f / K, k = f - t * K;
+                    const int t = (int)(((uint32_t)f * kdiv) >> 20), k = f - t * K;
                     if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = -1;
                 }
             } else {
@@ -477,21 +488,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (p.ln) {
                     // pass 2: biased variance about the mean (two-pass, as the reference)
                     float var[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int c = 0; c < p.tile_n; c += 32) {
-                        float v[32];
-                        tmem_ld32(lane_addr + c, v);
-                        const int g = c / W;
-                        const float mu = g == 0 ? mean[0] : g == 1 ? mean[1] : g == 2 ? mean[2] : mean[3];
-                        float s = 0.f;
+                    for (int c = 0; c < p.tile_n; c += 64) {  // tile_n and W are multiples of 32
+                        float v[64];
+                        if (c + 64 <= p.tile_n) {
+                            tmem_ld64(lane_addr + c, v);
+                        } else {
+                            float h[32];
+                            tmem_ld32(lane_addr + c, h);
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            const float d = v[e] - mu;
-                            s += d * d;
+                            for (int e = 0; e < 32; ++e) v[e] = h[e];
                         }
-                        var[0] += g == 0 ? s : 0.f;
-                        var[1] += g == 1 ? s : 0.f;
-                        var[2] += g == 2 ? s : 0.f;
-                        var[3] += g == 3 ? s : 0.f;
+#pragma unroll
+                        for (int half = 0; half < 2; ++half) {
+                            const int cc = c + 32 * half;
+                            if (cc >= p.tile_n) break;
+                            const int g = cc / W;
+                            const float mu = g == 0 ? mean[0] : g == 1 ? mean[1] : g == 2 ? mean[2] : mean[3];
+                            float s = 0.f;
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) {
+                                const float d = v[32 * half + e] - mu;
+                                s += d * d;
+                            }
+                            var[0] += g == 0 ? s : 0.f;
+                            var[1] += g == 1 ? s : 0.f;
+                            var[2] += g == 2 ? s : 0.f;
+                            var[3] += g == 3 ? s : 0.f;
+                        }
                     }
 #pragma unroll
                     for (int g = 0; g < 4; ++g) rstd[g] = 1.0f / sqrtf(var[g] / (float)W + p.eps);

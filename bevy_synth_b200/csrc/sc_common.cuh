@@ -70,9 +70,9 @@ template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
 // SiLU written from its definition x / (1 + e^{-x}) (reference:
-// burn_trellis sparse_decoder_wgpu_ops.rs:1713-1720); __expf is CUDA's
-// fast-math exponential intrinsic.
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// burn_trellis sparse_decoder_wgpu_ops.rs:1713-1720), evaluated with CUDA's
+// fast-math intrinsics __expf and __fdividef (results are stored as bf16).
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------- smem/mbar --
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -217,6 +217,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Two 32-column loads issued back to back, one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+    uint32_t r[64];
+#define SC_LD32(base, off)                                                                       \
+    asm volatile(                                                                                \
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                \
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"                                \
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"               \
+        : "=r"(r[base + 0]), "=r"(r[base + 1]), "=r"(r[base + 2]), "=r"(r[base + 3]),            \
+          "=r"(r[base + 4]), "=r"(r[base + 5]), "=r"(r[base + 6]), "=r"(r[base + 7]),            \
+          "=r"(r[base + 8]), "=r"(r[base + 9]), "=r"(r[base + 10]), "=r"(r[base + 11]),          \
+          "=r"(r[base + 12]), "=r"(r[base + 13]), "=r"(r[base + 14]), "=r"(r[base + 15]),        \
+          "=r"(r[base + 16]), "=r"(r[base + 17]), "=r"(r[base + 18]), "=r"(r[base + 19]),        \
+          "=r"(r[base + 20]), "=r"(r[base + 21]), "=r"(r[base + 22]), "=r"(r[base + 23]),        \
+          "=r"(r[base + 24]), "=r"(r[base + 25]), "=r"(r[base + 26]), "=r"(r[base + 27]),        \
+          "=r"(r[base + 28]), "=r"(r[base + 29]), "=r"(r[base + 30]), "=r"(r[base + 31])         \
+        : "r"(taddr + off))
+    SC_LD32(0, 0);
+    SC_LD32(32, 32);
+#undef SC_LD32
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
