@@ -27,7 +27,7 @@ DTYPE_BF16 = 1
 EXPORTED = (
     "sc_version", "sc_last_error", "sc_device_fault", "sc_kernel_rows", "sc_kernel_offsets",
     "sc_neighbor_workspace_bytes", "sc_neighbor_map", "sc_neighbor_map_query", "sc_neighbor_status",
-    "sc_neighbor_schedule_scratch_bytes", "sc_neighbor_schedule",
+    "sc_neighbor_map_noalloc", "sc_neighbor_schedule_scratch_bytes", "sc_neighbor_schedule",
     "sc_subm_conv_forward", "sc_conv_uses_tensor_cores", "sc_layer_norm_act", "sc_bf16_round",
     "sc_cast", "sc_subdivide_scratch_bytes", "sc_subdivide",
 )
@@ -84,6 +84,7 @@ _SIGS = {
     "sc_neighbor_map": ([_P, _P, _I64, _P, ctypes.c_size_t, _P, _P], ctypes.c_int),
     "sc_neighbor_map_query": ([_P, _P, _I64, _P, _I64, _P, ctypes.c_size_t, _P, _P], ctypes.c_int),
     "sc_neighbor_status": ([_P, ctypes.POINTER(ctypes.c_int32), _P], ctypes.c_int),
+    "sc_neighbor_map_noalloc": ([_P, _P, _I64, _P, _P], ctypes.c_int),
     "sc_neighbor_schedule_scratch_bytes": ([_I64, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "sc_neighbor_schedule": ([_P, _P, _I64, _P, ctypes.c_size_t, _P, _P, _P], ctypes.c_int),
     "sc_subm_conv_forward": ([_P, ctypes.c_int, _P, _I64, _P, _I64, _P, _P, _P, _P, _P], ctypes.c_int),

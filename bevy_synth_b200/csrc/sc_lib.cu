@@ -273,6 +273,36 @@ static int launch_simt(const sc_conv_config* c, const void* in, int64_t n_in, co
     return SC_OK;
 }
 
+// ---- static scratch of the no-allocation neighbor map ------------------------
+// Some callers cannot allocate device memory: they hold only the buffers they
+// pass in (their device memory belongs to another runtime's pool, e.g. a
+// burn/CubeCL backend that hands a custom op its input and output tensors and
+// nothing else), or they must not call cudaMalloc on their execution path.
+// sc_neighbor_map_noalloc serves them with this fixed table, which every GPU
+// that loads the library holds until process exit.
+constexpr int64_t kStaticTableSlots = int64_t(1) << 19;          // 8 MiB of 16-byte slots
+constexpr int64_t kStaticMaxRows = kStaticTableSlots / 2;        // 262,144 input rows
+constexpr size_t kStaticScratchBytes = 256 + (size_t)kStaticTableSlots * sizeof(HashSlot);
+static __device__ __align__(256) uint8_t g_nb_static_scratch[kStaticScratchBytes];
+
+// Device address of g_nb_static_scratch, resolved once per device with that
+// device current (in host code the symbol itself is only a host-side stand-in).
+static int static_scratch_address(void** out) {
+    static std::mutex mu;
+    static void* addr[128] = {nullptr};
+    int dev = 0;
+    SC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 128) return fail(SC_ERR_UNSUPPORTED, "device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        SC_CUDA_TRY(cudaGetSymbolAddress(&p, g_nb_static_scratch));
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return SC_OK;
+}
+
 }  // namespace sc
 
 using namespace sc;
@@ -365,6 +395,23 @@ int sc_neighbor_map_query(const sc_conv_config* cfg, const int32_t* in_coords, i
 int sc_neighbor_map(const sc_conv_config* cfg, const int32_t* coords, int64_t n, void* ws,
                     size_t ws_bytes, int32_t* out, void* stream) {
     return sc_neighbor_map_query(cfg, coords, n, coords, n, ws, ws_bytes, out, stream);
+}
+
+int sc_neighbor_map_noalloc(const sc_conv_config* cfg, const int32_t* coords, int64_t n, int32_t* out,
+                            void* stream) {
+    if (int rc = validate_config(cfg)) return rc;
+    if (n < 0) return fail(SC_ERR_INVALID, "negative row count");
+    if (n > kStaticMaxRows)
+        return fail(SC_ERR_CAPACITY, "sc_neighbor_map_noalloc: " + std::to_string(n) +
+                                         " rows exceed the static table limit of " +
+                                         std::to_string(kStaticMaxRows) + " rows");
+    if (n == 0) return SC_OK;
+    void* ws = nullptr;
+    if (int rc = static_scratch_address(&ws)) return rc;
+    // the allocating path's kernels on the static table; it clears the table
+    // and the status word at the start of every call
+    if (int rc = sc_neighbor_map_query(cfg, coords, n, coords, n, ws, kStaticScratchBytes, out, stream)) return rc;
+    return sc_neighbor_status(ws, nullptr, stream);
 }
 
 int sc_neighbor_status(const void* ws, int32_t* h_max_probe, void* stream) {

@@ -131,6 +131,25 @@ int sc_neighbor_map_query(const sc_conv_config* cfg, const int32_t* d_in_coords,
  * h_max_probe (nullable) receives the longest insert probe sequence. */
 int sc_neighbor_status(const void* d_workspace, int32_t* h_max_probe, void* stream);
 
+/* Neighbor map without any allocation, for callers that cannot allocate
+ * device memory: they hold only the buffers they pass in (for instance a
+ * burn/CubeCL backend whose device memory belongs to its own pool and which
+ * hands a custom op nothing but its input and output tensors), or they must
+ * not call cudaMalloc on their execution path.  Same result as
+ * sc_neighbor_map.  No counterpart in the reference.
+ *  - The hash table lives in a fixed 8 MiB static device array that every GPU
+ *    loading the library holds until exit; n_rows is limited to 262,144
+ *    (SC_ERR_CAPACITY beyond, checked before any GPU work).
+ *  - The first call on a device resolves the array's device address with
+ *    that device current; make that first call before any stream capture.
+ *  - Every call shares the one array and clears it first: calls that overlap
+ *    on the GPU (other streams, other host threads) race and must be
+ *    serialised by the caller.
+ *  - Synchronises `stream` to read the table status, as sc_neighbor_status
+ *    does, and returns SC_ERR_RANGE / SC_ERR_CAPACITY like it. */
+int sc_neighbor_map_noalloc(const sc_conv_config* cfg, const int32_t* d_coords, int64_t n_rows,
+                            int32_t* d_neighbor_rows, void* stream);
+
 /* Conv schedule of a neighbor map, computed once and reused by every conv on
  * the same map: a processing order of output rows that groups rows with equal
  * neighbor masks (valid-tap bit patterns) so that tensor-core tiles skip more
