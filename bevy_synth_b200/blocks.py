@@ -171,3 +171,27 @@ class UpsamplePyramid:
             x = res.forward(x, nbr)
             stats.append((coords.shape[0], nbr))
         return coords, x, stats
+
+
+class SubmStack:
+    """A chain of SubM3x3x3 layers with an optional SiLU after each (BASELINE
+    config 4: 8 x (SubM 512->512 + SiLU); config 5: 64->64, 64->256,
+    256->256, 256->256)."""
+
+    def __init__(self, weights: list, biases: list, silu: bool, device, dtype=torch.bfloat16):
+        self.w = [_dev(w, device, dtype) for w in weights]
+        self.b = [_dev(b, device, torch.float32) for b in biases]
+        self.cfgs = [F.SparseSubmConvConfig.subm3(w.shape[4], w.shape[0]) for w in weights]
+        self.silu = silu
+
+    def conv_count(self) -> int:
+        return len(self.w)
+
+    def forward(self, x: torch.Tensor, nbr: torch.Tensor, schedule=None) -> torch.Tensor:
+        for cfg, w, b in zip(self.cfgs, self.w, self.b):
+            x = F.sparse_subm_conv_forward(cfg, x, nbr, w, b, F.Epilogue(silu=self.silu, schedule=schedule))
+        return x
+
+    def flops(self, nbr: torch.Tensor) -> float:
+        p = float((nbr >= 0).sum())
+        return sum(2.0 * p * c.in_channels * c.out_channels for c in self.cfgs)

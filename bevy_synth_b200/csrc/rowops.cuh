@@ -83,6 +83,23 @@ __global__ void row_mask_key_kernel(const int32_t* __restrict__ nbr, int64_t n, 
     vals[r] = (int32_t)r;
 }
 
+// dst[i, :] = src[idx[i], :] for rows of `row_units` 16-byte units (halo packing).
+__global__ void gather_rows_kernel(const uint4* __restrict__ src, int64_t row_units,
+                                   const int32_t* __restrict__ idx, int64_t n, int64_t n_src,
+                                   uint4* __restrict__ dst) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * row_units) return;
+    const int64_t r = i / row_units;
+    const int64_t u = i - r * row_units;
+    const int32_t s = __ldg(idx + r);
+    if (s < 0 || s >= n_src) {
+        raise_fault(FAULT_BAD_NEIGHBOR);
+        dst[i] = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    dst[i] = __ldg(src + (int64_t)s * row_units + u);
+}
+
 // ordered[p, :] = nbr[order[p], :]
 __global__ void permute_rows_kernel(const int32_t* __restrict__ nbr, const int32_t* __restrict__ order,
                                     int64_t n, int K, int32_t* __restrict__ ordered) {

@@ -547,6 +547,20 @@ int sc_layer_norm_act(sc_dtype dtype, const void* x, int64_t rows, int64_t chann
     return SC_OK;
 }
 
+int sc_gather_rows(const void* src, int64_t n_src, int64_t row_bytes, const int32_t* idx, int64_t n, void* dst,
+                   void* stream) {
+    if (n < 0 || n_src < 0 || row_bytes <= 0) return fail(SC_ERR_INVALID, "invalid gather shape");
+    if (row_bytes % 16 != 0) return fail(SC_ERR_UNSUPPORTED, "gather rows must be a multiple of 16 bytes");
+    if (n == 0) return SC_OK;
+    if (!src || !idx || !dst || !aligned16(src) || !aligned16(dst))
+        return fail(SC_ERR_INVALID, "null or unaligned gather pointer");
+    const int64_t units = row_bytes / 16;
+    gather_rows_kernel<<<grid1d(n * units, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(src), units, idx, n, n_src, static_cast<uint4*>(dst));
+    SC_CUDA_TRY(cudaGetLastError());
+    return SC_OK;
+}
+
 int sc_bf16_round(const float* x, int64_t n, float* y, void* stream) {
     if (n < 0) return fail(SC_ERR_INVALID, "negative length");
     if (n == 0) return SC_OK;

@@ -326,6 +326,19 @@ def bf16_round_to_f32(x: torch.Tensor) -> torch.Tensor:
     return y
 
 
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[i] = src[idx[i]] (rows of a contiguous 2-D CUDA tensor)."""
+    _require_cuda("src", src)
+    _require_cuda("idx", idx)
+    if idx.dtype != torch.int32:
+        raise SparseConvError(_lib.SC_ERR_INVALID, "gather index dtype must be I32")
+    if out is None:
+        out = torch.empty((idx.shape[0],) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+    row_bytes = src[0].numel() * src.element_size() if src.shape[0] else out[0].numel() * out.element_size()
+    check(lib().sc_gather_rows(_ptr(src), src.shape[0], row_bytes, _ptr(idx), idx.shape[0], _ptr(out), _stream(src)))
+    return out
+
+
 def cast(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     _require_cuda("input", x)
     y = torch.empty(x.shape, dtype=dtype, device=x.device)

@@ -39,8 +39,16 @@ def morton_sort(coords: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(c[order])
 
 
+def _unique_xyz(xyz: np.ndarray) -> np.ndarray:
+    """Unique rows of non-negative [M,3] int coordinates (< 2^21 each), via 1-D keys."""
+    xyz = np.asarray(xyz, np.int64).reshape(-1, 3)
+    key = np.unique((xyz[:, 0] << 42) | (xyz[:, 1] << 21) | xyz[:, 2])
+    mask = (1 << 21) - 1
+    return np.stack([key >> 42, (key >> 21) & mask, key & mask], axis=1).astype(np.int32)
+
+
 def unique_cells(batch: int, xyz: np.ndarray) -> np.ndarray:
-    xyz = np.unique(np.asarray(xyz, np.int32).reshape(-1, 3), axis=0)
+    xyz = _unique_xyz(xyz)
     b = np.full((xyz.shape[0], 1), batch, np.int32)
     return np.concatenate([b, xyz], axis=1)
 
@@ -99,7 +107,7 @@ def ellipsoid_shell(grid: int, centre, axes, half_thickness: float) -> np.ndarra
         cand.append(np.stack([xs[idx], ys[idx], zz], axis=1))
     if not cand:
         return np.zeros((0, 3), np.int32)
-    c = np.unique(np.concatenate(cand), axis=0)
+    c = _unique_xyz(np.concatenate(cand)).astype(np.int64)
     u = (c + 0.5 - p) / a
     rho = np.sqrt((u ** 2).sum(1))
     g = np.sqrt(((u / a) ** 2).sum(1)) / np.maximum(rho, 1e-12)
@@ -231,13 +239,12 @@ def config5_coords(seed: int = 0, shells: int = 32, grid: int = 1024,
 
 
 def config5(seed: int = 0, grid: int = 1024, shells: int = 32) -> Workload:
-    """2 x SubM 64->64 then 2 x SubM 256->256 on the 1024^3 union of shells.
-    The C=64 output is widened to 256 channels by repeat-interleave x4 (the
-    decoder's skip-path widening) before the C=256 layers."""
+    """Four SubM layers on the 1024^3 union of shells: two read C=64 features
+    (64->64, 64->256) and two read C=256 (256->256, 256->256)."""
     rng = np.random.default_rng(seed)
     coords = config5_coords(seed, shells, grid)
     feats = rng.standard_normal((coords.shape[0], 64)).astype(np.float32)
-    chans = [(64, 64), (64, 64), (256, 256), (256, 256)]
+    chans = [(64, 64), (64, 256), (256, 256), (256, 256)]
     ws = [normal_weight(rng, co, ci) for ci, co in chans]
     bs = [np.zeros(co, np.float32) for _, co in chans]
     return Workload("cfg5_sharded_grid_bf16", coords, feats, {"w": ws, "b": bs, "chans": chans}, {})

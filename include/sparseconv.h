@@ -185,6 +185,13 @@ int sc_conv_uses_tensor_cores(const sc_conv_config* cfg, sc_dtype dtype, int32_t
 int sc_layer_norm_act(sc_dtype dtype, const void* d_x, int64_t rows, int64_t channels,
                       const float* d_gamma, const float* d_beta, float eps, int32_t layer_norm,
                       int32_t silu, void* d_y, void* stream);
+/* dst[i] = src[idx[i]] for n rows of row_bytes (a multiple of 16) each: packs
+ * the boundary rows another rank needs (halo exchange).  Indices outside
+ * [0, n_src) give zero rows and raise the device fault word.  Plays the role
+ * of burn's Tensor::select by row index (crates/burn_trellis/src/runtime_model/
+ * sparse_decoder_runtime_impl.rs:2249-2255). */
+int sc_gather_rows(const void* d_src, int64_t n_src, int64_t row_bytes, const int32_t* d_idx, int64_t n,
+                   void* d_dst, void* stream);
 /* fp32 -> fp32 rounded to bf16 (RNE, no NaN special case). */
 int sc_bf16_round(const float* d_x, int64_t n, float* d_y, void* stream);
 /* fp32 <-> bf16 storage conversion (RNE). */
