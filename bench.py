@@ -335,7 +335,7 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "tflops": tflops, "pct_bf16_peak": tflops / peak_tf,
+            "tflops": tflops, "pct_bf16_peak": tflops / (peak_tf * world),
             "config": {"workload": wl.name, "voxels_per_gpu": n, "voxels_total": n_all, "blocks": len(wl.params),
                        "channels": c, "convs_per_step": convs, "valid_pairs_P": P,
                        "step": "neighbor map + row order + LN1/SiLU + 8 fused SubM convs",
