@@ -26,6 +26,14 @@
 //   warp 4+PW          MMA issuer (one thread).
 // The accumulator is double-buffered in TMEM (2 x 256 columns) when
 // tile_n <= 256, so the epilogue of one tile overlaps the MMAs of the next.
+//
+// PAIR (2-SM) variant, launched as clusters of two CTAs: a tile is 256 rows,
+// 128 per CTA; the leader issues tcgen05.mma.cta_group::2 with M = 256, each
+// CTA's A from its own shared memory and B split by N across the pair, so a
+// CTA loads and the tensor cores read only half of every weight tile (the
+// single-CTA kernel's shared-memory traffic is its limit).  Both halves of B
+// arrive by TMA on the leader's full barrier; the peer's "A landed" is relayed
+// by its otherwise idle MMA warp; commits are multicast to both CTAs.
 // Every mbarrier wait is bounded: on expiry the device fault word is raised
 // and the CTA drains and exits instead of hanging.
 #pragma once
@@ -162,6 +170,7 @@ __device__ __forceinline__ void add_param32(float (&v)[32], const float* p, bool
     }
 }
 
+template <bool PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -169,7 +178,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int S = p.stages;
     const int K = p.K;
-    const int B_BYTES = p.tile_n * 128;
+    // PAIR: a CTA holds half of every MMA's B rows (the pair splits N)
+    const int B_ROWS = PAIR ? p.sub_n / 2 : p.sub_n;        // per sub-MMA, in this CTA
+    const int B_BYTES = p.n_sub * B_ROWS * 128;            // per stage, in this CTA
     const int stg_cols = p.stg_cols;
     const int stg_units = stg_cols / 8;
     uint8_t* a_smem = smem;
@@ -177,39 +188,53 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint8_t* stg_smem = b_smem + S * B_BYTES;                                    // 4 warps
     int32_t* nbr_s = reinterpret_cast<int32_t*>(stg_smem + 4 * 32 * (stg_units + 1) * 16);  // [TC_BM][K]
     uint64_t* bars = reinterpret_cast<uint64_t*>(nbr_s + TC_BM * K);
-    uint64_t* full = bars;
-    uint64_t* empty = bars + S;
-    uint64_t* tmem_full = bars + 2 * S;   // [2]
-    uint64_t* tmem_empty = bars + 2 * S + 2;
-    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);  // [S]
+    uint64_t* full = bars;                 // [S] MMA may read the stage (leader / single CTA)
+    uint64_t* afull = bars + S;            // [S] PAIR peer: this CTA's A copies have landed
+    uint64_t* empty = bars + 2 * S;        // [S] the MMAs reading the stage are done
+    uint64_t* tmem_full = bars + 3 * S;    // [2]
+    uint64_t* tmem_empty = bars + 3 * S + 2;
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);  // [S]
     uint32_t* misc = stage_flags + S;     // [0] tmem base, [1] abort
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int64_t my_tiles = p.n_tiles > (int64_t)blockIdx.x ? (p.n_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    const int64_t unit = PAIR ? (int64_t)(blockIdx.x >> 1) : (int64_t)blockIdx.x;
+    const int64_t n_units = PAIR ? (int64_t)(gridDim.x >> 1) : (int64_t)gridDim.x;
+    constexpr int TILE_ROWS = PAIR ? 2 * TC_BM : TC_BM;
+    const int64_t my_tiles = p.n_tiles > unit ? (p.n_tiles - 1 - unit) / n_units + 1 : 0;
     const int n_chunks = (p.cin + TC_BK - 1) / TC_BK;
     constexpr int MMA_WARP = 4 + TC_PW;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], TC_PW * 32 + 1);  // gather lanes (async) + the TMA/flags arrive
-            mbar_init(&empty[s], 1);              // one tcgen05.commit
+            // gather lanes (async, .noinc) + the producer's expect_tx arrive (+ the peer's relay)
+            mbar_init(&full[s], TC_PW * 32 + 1 + (PAIR ? 1 : 0));
+            mbar_init(&afull[s], TC_PW * 32 + 1);   // PAIR peer: gather lanes + the flags arrive
+            mbar_init(&empty[s], 1);                // one tcgen05.commit
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&tmem_full[b], 1);          // tcgen05.commit after a tile's last MMA
-            mbar_init(&tmem_empty[b], 4);         // one arrive per epilogue warp
+            mbar_init(&tmem_full[b], 1);            // tcgen05.commit after a tile's last MMA
+            mbar_init(&tmem_empty[b], PAIR ? 8 : 4);  // one arrive per epilogue warp (of both CTAs)
         }
         misc[1] = 0;
         fence_mbar_init();
         fence_proxy_async_smem();
     }
     if (warp == MMA_WARP) {
-        tmem_alloc(&misc[0], TC_TMEM_COLS);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(&misc[0], TC_TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(&misc[0], TC_TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     if (warp == 4 && lane == 0) tma_prefetch_desc(&wmap);
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // the peer's barriers exist before any remote arrive / TMA
     tc_fence_after();
     const uint32_t tmem_base = misc[0];
     volatile uint32_t* abort_flag = &misc[1];
@@ -222,23 +247,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         constexpr int ROWS = TC_BM / TC_PW;     // rows per producer warp
         constexpr int GROUPS = ROWS / 4;        // copy instructions per stage
         int32_t* my_nbr = nbr_s + pw * ROWS * K;
-        int it = 0;
+        const int own0 = (int)rank * TC_BM + pw * ROWS;  // my rows within the tile
+        uint64_t* arrive_bar = (PAIR && !leader) ? afull : full;
+        const uint32_t leader_full0 = PAIR ? mapa_shared(smem_u32(full), 0) : 0u;
+        int s = 0;          // stage ring position and its phase bit
+        uint32_t ph = 0;
         bool ok = true;
         for (int64_t lt = 0; lt < my_tiles && ok; ++lt) {
-            const int64_t tile = blockIdx.x + lt * gridDim.x;
-            const int64_t tile_base = (tile / p.grid_y) * TC_BM;
+            const int64_t tile = unit + lt * n_units;
+            const int64_t tile_row0 = (tile / p.grid_y) * TILE_ROWS;
             const int n0 = (int)(tile % p.grid_y) * p.tile_n;
-            // neighbor rows of the whole tile (for the common tap mask), mine kept in smem
+            // neighbor rows of the whole tile (the common tap mask), mine kept in smem
             uint32_t mask = 0;
-            const int64_t n_valid = p.n_rows - tile_base < TC_BM ? p.n_rows - tile_base : TC_BM;
+            const int64_t n_valid = p.n_rows - tile_row0 < TILE_ROWS ? p.n_rows - tile_row0 : TILE_ROWS;
             const int n_ints = (int)n_valid * K;
+            const uint64_t kdiv = (1ull << 32) / (uint64_t)K + 1ull;  // f / K == (f * kdiv) >> 32 here
             if (p.row_order == nullptr || p.nbr_ordered != nullptr) {
                 // the tile's map rows are contiguous: independent 16-byte loads,
                 // issued 8 deep before any is consumed (one latency per batch)
-                const int32_t* blk = (p.nbr_ordered ? p.nbr_ordered : p.nbr) + tile_base * K;
+                const int32_t* blk = (p.nbr_ordered ? p.nbr_ordered : p.nbr) + tile_row0 * K;
                 const int n_full = n_ints / 4;               // whole int4 vectors
                 const int n_vec = (n_ints + 3) / 4;
-                const uint32_t kdiv = (1u << 20) / (uint32_t)K + 1u;  // f / K == (f * kdiv) >> 20 here
                 for (int base = 0; base < n_vec; base += 8 * 32) {
                     int4 q[8];
 #pragma unroll
@@ -261,28 +290,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         for (int e = 0; e < 4; ++e) {
                             const int f = 4 * f4 + e;
                             if (f >= n_ints) break;
-                            const int t = (int)(((uint32_t)f * kdiv) >> 20), k = f - t * K;
+                            const int t = (int)(((uint64_t)f * kdiv) >> 32), k = f - t * K;
                             int32_t v = vals[e];
                             if (v < -1 || v >= p.n_in) {
                                 raise_fault(FAULT_BAD_NEIGHBOR);
                                 v = -1;
                             }
                             if (v >= 0) mask |= 1u << k;
-                            if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = v;
+                            if (t >= own0 && t < own0 + ROWS) my_nbr[(t - own0) * K + k] = v;
                         }
                     }
                 }
-                for (int f = n_ints + lane; f < TC_BM * K; f += 32) {
-                    const int t = (int)(((uint32_t)f * kdiv) >> 20), k = f - t * K;
-                    if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = -1;
+                for (int f = lane; f < ROWS * K; f += 32) {  // my rows past the end of the grid
+                    const int t = (int)(((uint64_t)f * kdiv) >> 32);
+                    if (own0 + t >= n_valid) my_nbr[f] = -1;
                 }
             } else {
                 // row order without a pre-ordered map: gather the rows
-                for (int i = lane; i < TC_BM * K; i += 32) {
-                    const int t = i / K, k = i - t * K;
+                for (int i = lane; i < TILE_ROWS * K; i += 32) {
+                    const int t = (int)(((uint64_t)i * kdiv) >> 32), k = i - t * K;
                     int32_t v = -1;
                     if (i < n_ints) {
-                        const int64_t r = ordered_row(p.row_order, tile_base + t, p.n_rows);
+                        const int64_t r = ordered_row(p.row_order, tile_row0 + t, p.n_rows);
                         if (r >= 0) {
                             v = __ldg(p.nbr + r * K + k);
                             if (v < -1 || v >= p.n_in) {
@@ -292,7 +321,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                     }
                     if (v >= 0) mask |= 1u << k;
-                    if (t >= pw * ROWS && t < (pw + 1) * ROWS) my_nbr[(t - pw * ROWS) * K + k] = v;
+                    if (t >= own0 && t < own0 + ROWS) my_nbr[(t - own0) * K + k] = v;
                 }
             }
             mask = __reduce_or_sync(0xffffffffu, mask);
@@ -306,19 +335,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                 for (int i = 0; i < GROUPS; ++i) src[i] = my_nbr[(i * 4 + sub) * K + k];
                 for (int ch = 0; ch < n_chunks; ++ch, ++step) {
-                    const int s = it % S;
-                    const uint32_t ph = (uint32_t)(it / S) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u)) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u))) {
                         ok = false;
                         break;
                     }
                     if (pw == 0 && lane == 0) {
                         stage_flags[s] = (step == 0 ? 1u : 0u) | (step == n_steps - 1 ? 2u : 0u);
-                        mbar_arrive_expect_tx(&full[s], (uint32_t)B_BYTES);
                         const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
-                        for (int q = 0; q < p.n_sub; ++q)
-                            tma_load_3d(dst + q * p.sub_n * 128, &wmap, &full[s], ch * TC_BK, k,
-                                        n0 + q * p.sub_n);
+                        if (!PAIR) {
+                            mbar_arrive_expect_tx(&full[s], (uint32_t)B_BYTES);
+                            for (int q = 0; q < p.n_sub; ++q)
+                                tma_load_3d(dst + q * B_ROWS * 128, &wmap, &full[s], ch * TC_BK, k,
+                                            n0 + q * p.sub_n);
+                        } else {
+                            // both halves of B complete on the leader's full barrier
+                            if (leader) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * B_BYTES));
+                            const uint32_t bar = leader_full0 + (uint32_t)(s * 8);
+                            for (int q = 0; q < p.n_sub; ++q)
+                                tma_load_3d_pair(dst + q * B_ROWS * 128, &wmap, bar, ch * TC_BK, k,
+                                                 n0 + q * p.sub_n + (int)rank * B_ROWS);
+                            if (!leader) mbar_arrive(&afull[s]);  // publishes stage_flags to the relay
+                        }
                     }
                     const int c = ch * TC_BK + j * 8;
                     const uint32_t stage = smem_u32(a_smem + s * TC_A_BYTES);
@@ -329,18 +366,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         const void* g = v ? (const void*)(p.in + (int64_t)src[i] * p.cin + c) : (const void*)p.in;
                         cp_async_16(stage + r * 128 + ((j ^ (r & 7)) << 4), g, v ? 16u : 0u);
                     }
-                    cp_async_arrive_noinc(&full[s]);
-                    ++it;
+                    cp_async_arrive_noinc(&arrive_bar[s]);
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                 }
             }
         }
         cp_async_wait<0>();
         if (!ok) *abort_flag = 1u;
     } else if (warp == MMA_WARP) {
-        // ====================================================== MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = umma_idesc_bf16_m128((uint32_t)p.sub_n);
-            int it = 0;
+        if (PAIR && !leader) {
+            // ================================================ relay (pair peer)
+            // forwards "this CTA's A stage has landed" to the leader's full barrier
+            if (lane == 0) {
+                const uint32_t leader_full0 = mapa_shared(smem_u32(full), 0);
+                int s = 0;
+                uint32_t ph = 0;
+                for (int64_t lt = 0; lt < my_tiles;) {
+                    if (!mbar_wait(&afull[s], ph)) {
+                        *abort_flag = 1u;
+                        break;
+                    }
+                    const uint32_t flags = stage_flags[s];
+                    fence_proxy_async_smem();  // cp.async data -> the tensor core's reads
+                    mbar_arrive_cluster(leader_full0 + (uint32_t)(s * 8));
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                    if (flags & 2u) ++lt;
+                }
+            }
+        } else if (lane == 0) {
+            // ================================================ MMA issuer
+            const uint32_t idesc = PAIR ? umma_idesc_bf16_m256((uint32_t)p.sub_n) : umma_idesc_bf16_m128((uint32_t)p.sub_n);
+            int s = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (int64_t lt = 0; lt < my_tiles && ok; ++lt) {
                 const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
@@ -353,8 +416,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const uint32_t acc = tmem_base + (uint32_t)(b * 256);
                 bool first = true;
                 for (;;) {
-                    const int s = it % S;
-                    const uint32_t ph = (uint32_t)(it / S) & 1u;
                     if (!mbar_wait(&full[s], ph)) {
                         ok = false;
                         break;
@@ -368,17 +429,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
                         const uint64_t ad = umma_desc_sw128(a0 + kk * 32);
                         for (int q = 0; q < p.n_sub; ++q) {
-                            const uint64_t bd = umma_desc_sw128(b0 + q * p.sub_n * 128 + kk * 32);
-                            umma_bf16(acc + q * p.sub_n, ad, bd, idesc, (first && kk == 0) ? 0u : 1u);
+                            const uint64_t bd = umma_desc_sw128(b0 + q * B_ROWS * 128 + kk * 32);
+                            if (PAIR)
+                                umma_bf16_pair(acc + q * p.sub_n, ad, bd, idesc, (first && kk == 0) ? 0u : 1u);
+                            else
+                                umma_bf16(acc + q * p.sub_n, ad, bd, idesc, (first && kk == 0) ? 0u : 1u);
                         }
                     }
-                    umma_commit(&empty[s]);
-                    ++it;
+                    if (PAIR)
+                        umma_commit_pair(&empty[s], 0x3);
+                    else
+                        umma_commit(&empty[s]);
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                     first = false;
                     if (flags & 2u) break;
                 }
                 if (!ok) break;
-                umma_commit(&tmem_full[b]);
+                if (PAIR)
+                    umma_commit_pair(&tmem_full[b], 0x3);
+                else
+                    umma_commit(&tmem_full[b]);
             }
             if (!ok) *abort_flag = 1u;
         }
@@ -387,13 +460,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         Staging st;
         st.units = stg_units;
         st.base = stg_smem + warp * 32 * (stg_units + 1) * 16;
-        const int t = tid;  // TMEM lane == tile row
+        const int t = tid;  // TMEM lane == tile row (of this CTA's half)
         const int W = p.ln_width;
         const bool multi = p.ln != 0 || p.out2 != nullptr;
         const bool dense_res = p.residual != nullptr && p.res_off == nullptr;
+        const uint32_t leader_tmem_empty = PAIR ? mapa_shared(smem_u32(tmem_empty), 0) : 0u;
         for (int64_t lt = 0; lt < my_tiles; ++lt) {
-            const int64_t tile = blockIdx.x + lt * gridDim.x;
-            const int64_t tile_base = (tile / p.grid_y) * TC_BM;
+            const int64_t tile = unit + lt * n_units;
+            const int64_t tile_base = (tile / p.grid_y) * TILE_ROWS + (int64_t)rank * TC_BM;
             const int n0 = (int)(tile % p.grid_y) * p.tile_n;
             const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
             const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
@@ -561,15 +635,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty[b]);
+            if (lane == 0) {
+                if (PAIR && !leader)
+                    mbar_arrive_cluster(leader_tmem_empty + (uint32_t)(b * 8));
+                else
+                    mbar_arrive(&tmem_empty[b]);
+            }
         }
     }
 
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // no CTA leaves while its pair may still touch its barriers
     if (warp == MMA_WARP) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TC_TMEM_COLS);
+        if (PAIR)
+            tmem_dealloc_pair(tmem_base, TC_TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, TC_TMEM_COLS);
     }
 }
 
@@ -581,11 +664,13 @@ inline int tc_stg_cols(int tile_n) {
     return 32;
 }
 
-// Dynamic shared-memory bytes of a launch (1 KB alignment slack included).
-inline size_t tc_smem_bytes(int stages, int tile_n, int K) {
+// Dynamic shared-memory bytes of a launch (1 KB alignment slack included);
+// with `pair`, a CTA holds half of the B rows.
+inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair) {
     const int stg_cols = tc_stg_cols(tile_n);
-    return 1024 + (size_t)stages * (TC_A_BYTES + (size_t)tile_n * 128) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
-           (size_t)TC_BM * K * 4 + (2 * stages + 4) * 8 + stages * 4 + 16;
+    const size_t b_bytes = (size_t)(pair ? tile_n / 2 : tile_n) * 128;
+    return 1024 + (size_t)stages * (TC_A_BYTES + b_bytes) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
+           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 16;
 }
 
 }  // namespace sc

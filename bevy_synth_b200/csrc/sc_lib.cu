@@ -101,8 +101,16 @@ static bool force_simt() {
 
 struct TcPlan {
     int tile_n, n_sub, sub_n, stages, grid_y, n_buf;
+    bool pair;  // 2-SM (cta_group::2) kernel on CTA pairs
     size_t smem;
 };
+
+// The CTA-pair (2-SM) kernel is opt-in (SC_TC_PAIR=1) until it is the faster
+// one on the measured workloads; the single-CTA kernel is the default.
+static bool allow_pair() {
+    const char* e = std::getenv("SC_TC_PAIR");
+    return e && e[0] == '1';
+}
 
 static constexpr size_t kMaxDynSmem = 232448;  // 227 KB opt-in per block on sm_100
 
@@ -146,15 +154,16 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     if (plan->sub_n % 16 != 0) return false;
     plan->n_buf = tile_n <= 256 ? 2 : 1;
     plan->grid_y = (int)(cout / tile_n);
+    plan->pair = allow_pair() && plan->sub_n >= 32;
     int S = 8;
-    while (S >= 2 && tc_smem_bytes(S, tile_n, (int)K) > kMaxDynSmem) --S;
+    while (S >= 2 && tc_smem_bytes(S, tile_n, (int)K, plan->pair) > kMaxDynSmem) --S;
     if (const char* env = std::getenv("SC_TC_STAGES")) {  // tuning override, clamped to what fits
         const int want = std::atoi(env);
         if (want >= 2 && want < S) S = want;
     }
     if (S < 2) return false;
     plan->stages = S;
-    plan->smem = tc_smem_bytes(S, tile_n, (int)K);
+    plan->smem = tc_smem_bytes(S, tile_n, (int)K, plan->pair);
     return true;
 }
 
@@ -167,7 +176,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     CUtensorMap wmap;
     cuuint64_t dims[3] = {(cuuint64_t)cin, (cuuint64_t)K, (cuuint64_t)cout};
     cuuint64_t strides[2] = {(cuuint64_t)cin * 2, (cuuint64_t)(K * cin * 2)};
-    cuuint32_t box[3] = {(cuuint32_t)TC_BK, 1u, (cuuint32_t)plan.sub_n};
+    cuuint32_t box[3] = {(cuuint32_t)TC_BK, 1u, (cuuint32_t)(plan.pair ? plan.sub_n / 2 : plan.sub_n)};
     cuuint32_t estr[3] = {1u, 1u, 1u};
     CUresult r = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(w), dims, strides,
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -191,7 +200,8 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     p.stages = plan.stages;
     p.n_buf = plan.n_buf;
     p.grid_y = plan.grid_y;
-    p.n_tiles = ((n_rows + TC_BM - 1) / TC_BM) * plan.grid_y;
+    const int64_t tile_rows = plan.pair ? 2 * TC_BM : TC_BM;
+    p.n_tiles = ((n_rows + tile_rows - 1) / tile_rows) * plan.grid_y;
     p.stg_cols = tc_stg_cols(plan.tile_n);
     if (p.stg_cols % 32 != 0 || plan.tile_n % p.stg_cols != 0)
         return fail(SC_ERR_UNSUPPORTED, "internal: staging width does not tile the output tile");
@@ -214,12 +224,38 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_err = cudaFuncSetAttribute(conv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)kMaxDynSmem);
+        if (attr_err == cudaSuccess)
+            attr_err = cudaFuncSetAttribute(conv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)kMaxDynSmem);
     });
     SC_CUDA_TRY(attr_err);
-    const int64_t ctas = std::min<int64_t>(p.n_tiles, sm_count());
-    conv_tc_kernel<<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, p);
+    if (!plan.pair) {
+        const int64_t ctas = std::min<int64_t>(p.n_tiles, sm_count());
+        conv_tc_kernel<false><<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, p);
+    } else {
+        cudaLaunchConfig_t lc;
+        memset(&lc, 0, sizeof lc);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        lc.blockDim = dim3(TC_THREADS);
+        lc.dynamicSmemBytes = plan.smem;
+        lc.stream = st;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        lc.gridDim = dim3((unsigned)(2 * sm_count()));
+        int max_clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&max_clusters, conv_tc_kernel<true>, &lc) != cudaSuccess ||
+            max_clusters <= 0)
+            max_clusters = sm_count() / 2;
+        const int64_t pairs = std::min<int64_t>(p.n_tiles, max_clusters);
+        lc.gridDim = dim3((unsigned)(2 * pairs));
+        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true>, wmap, p));
+    }
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
 }

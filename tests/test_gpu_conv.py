@@ -314,3 +314,49 @@ def test_bf16_epilogue_writes_stay_inside_rows(cuda_device, c):
     plain = F.sparse_subm_conv_forward(cfg, to_dev(x, BF16), nbr, to_dev(w, BF16), to_dev(b))
     assert rel_l2(plain.float().cpu().numpy(), bf16_ref(cfg, x, w, b, nbr.cpu().numpy())) <= 4e-3
     assert_no_fault()
+
+
+@pytest.mark.parametrize("cin,cout,mode", [(64, 64, "plain"), (96, 96, "ln"), (192, 192, "res_out2"),
+                                           (256, 256, "res_out2"), (384, 384, "ln"), (512, 512, "plain"),
+                                           (128, 512, "rowmap")])
+def test_pair_and_single_cta_kernels_agree(cuda_device, monkeypatch, cin, cout, mode):
+    """The 2-SM (CTA pair) kernel against the single-CTA kernel on the same
+    inputs: identical arithmetic per row, so results agree to rounding."""
+    coords = shell()
+    n = coords.shape[0]
+    rng = np.random.default_rng(cin + cout)
+    x = to_dev(rng.standard_normal((n, cin)).astype(np.float32), BF16)
+    w = to_dev((rng.standard_normal((cout, 3, 3, 3, cin)) * 0.03).astype(np.float32), BF16)
+    b = to_dev((0.1 * rng.standard_normal(cout)).astype(np.float32))
+    cfg = F.SparseSubmConvConfig.subm3(cin, cout)
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords))
+
+    def run():
+        kw, extra = {}, {}
+        if mode == "ln":
+            epi = F.Epilogue(layer_norm=True, ln_eps=1e-5, silu=True)
+        elif mode == "res_out2":
+            res = to_dev(rng.standard_normal((n, cout)).astype(np.float32), BF16)
+            extra["out2"] = torch.empty((n, cout), dtype=BF16, device="cuda:0")
+            epi = F.Epilogue(residual=res, layer_norm=True, ln_eps=1e-5, silu=True, out2=extra["out2"])
+        elif mode == "rowmap":
+            mask = to_dev((np.random.default_rng(1).random((n, 8)) < 0.5).astype(np.uint8))
+            child_row, child_coords, _ = F.subdivide(to_dev(coords), mask, cin)
+            kw["out_rows"] = child_coords.shape[0]
+            epi = F.Epilogue(layer_norm=True, ln_width=cout // 8, ln_eps=1e-6, silu=True, out_row_map=child_row,
+                             out_row_map_cols=8)
+        else:
+            epi = F.Epilogue(schedule=F.neighbor_schedule(cfg, nbr))
+        y = F.sparse_subm_conv_forward(cfg, x, nbr, w, b, epi, **kw)
+        outs = [y.float().cpu()] + ([extra["out2"].float().cpu()] if "out2" in extra else [])
+        return outs
+
+    rng_state = rng.bit_generator.state
+    monkeypatch.setenv("SC_TC_PAIR", "1")
+    pair = run()
+    rng.bit_generator.state = rng_state
+    monkeypatch.setenv("SC_TC_PAIR", "0")
+    single = run()
+    for a, s in zip(pair, single):
+        assert rel_l2(a.numpy(), s.numpy()) <= 1e-6
+    assert_no_fault()
