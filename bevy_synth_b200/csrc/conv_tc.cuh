@@ -193,8 +193,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t* empty = bars + 2 * S;        // [S] the MMAs reading the stage are done
     uint64_t* tmem_full = bars + 3 * S;    // [2]
     uint64_t* tmem_empty = bars + 3 * S + 2;
-    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);  // [S]
-    uint32_t* misc = stage_flags + S;     // [0] tmem base, [1] abort
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);  // [S] PAIR relay: last step of a tile
+    uint32_t* tile_steps = stage_flags + S;  // [8] reduction steps per tile, ring over tiles
+    // (the producers run at most S <= 8 stages, so at most 8 one-step tiles, ahead of the MMA thread)
+    uint32_t* misc = tile_steps + 8;      // [0] tmem base, [1] abort
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -340,7 +342,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         break;
                     }
                     if (pw == 0 && lane == 0) {
-                        stage_flags[s] = (step == 0 ? 1u : 0u) | (step == n_steps - 1 ? 2u : 0u);
+                        // published to the MMA thread by this stage's full-barrier arrive below
+                        if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
+                        stage_flags[s] = step == n_steps - 1 ? 2u : 0u;
                         const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
                         if (!PAIR) {
                             mbar_arrive_expect_tx(&full[s], (uint32_t)B_BYTES);
@@ -401,7 +405,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         } else if (lane == 0) {
             // ================================================ MMA issuer
+            // The tensor pipe's queue is short: this loop is kept to wait,
+            // fence, four MMAs and a commit per stage.
             const uint32_t idesc = PAIR ? umma_idesc_bf16_m256((uint32_t)p.sub_n) : umma_idesc_bf16_m128((uint32_t)p.sub_n);
+            const uint64_t adesc0 = umma_desc_sw128(smem_u32(a_smem));
+            const uint64_t bdesc0 = umma_desc_sw128(smem_u32(b_smem));
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
@@ -414,26 +422,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t acc = tmem_base + (uint32_t)(b * 256);
-                bool first = true;
-                for (;;) {
+                uint32_t steps = 0;
+                for (uint32_t step = 0;; ++step) {
                     if (!mbar_wait(&full[s], ph)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     fence_proxy_async_smem();  // cp.async (generic proxy) data -> tcgen05.mma reads
-                    const uint32_t flags = stage_flags[s];
-                    const uint32_t a0 = smem_u32(a_smem + s * TC_A_BYTES);
-                    const uint32_t b0 = smem_u32(b_smem + s * B_BYTES);
+                    if (step == 0) steps = tile_steps[lt & 7];
+                    const uint64_t ad = adesc0 + (uint64_t)((s * TC_A_BYTES) >> 4);
+                    const uint64_t bd = bdesc0 + (uint64_t)((s * B_BYTES) >> 4);
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                        const uint64_t ad = umma_desc_sw128(a0 + kk * 32);
                         for (int q = 0; q < p.n_sub; ++q) {
-                            const uint64_t bd = umma_desc_sw128(b0 + q * B_ROWS * 128 + kk * 32);
+                            const uint64_t bq = bd + (uint64_t)((q * B_ROWS * 128 + kk * 32) >> 4);
+                            const uint32_t accum = (step == 0 && kk == 0) ? 0u : 1u;
                             if (PAIR)
-                                umma_bf16_pair(acc + q * p.sub_n, ad, bd, idesc, (first && kk == 0) ? 0u : 1u);
+                                umma_bf16_pair(acc + q * p.sub_n, ad + (uint64_t)(kk * 2), bq, idesc, accum);
                             else
-                                umma_bf16(acc + q * p.sub_n, ad, bd, idesc, (first && kk == 0) ? 0u : 1u);
+                                umma_bf16(acc + q * p.sub_n, ad + (uint64_t)(kk * 2), bq, idesc, accum);
                         }
                     }
                     if (PAIR)
@@ -444,8 +452,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         s = 0;
                         ph ^= 1u;
                     }
-                    first = false;
-                    if (flags & 2u) break;
+                    if (step + 1 >= steps) break;
                 }
                 if (!ok) break;
                 if (PAIR)
@@ -670,7 +677,7 @@ inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair) {
     const int stg_cols = tc_stg_cols(tile_n);
     const size_t b_bytes = (size_t)(pair ? tile_n / 2 : tile_n) * 128;
     return 1024 + (size_t)stages * (TC_A_BYTES + b_bytes) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
-           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 16;
+           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16;
 }
 
 }  // namespace sc
