@@ -49,6 +49,7 @@ constexpr int TC_PW = 2;                       // gather producer warps
 constexpr int TC_THREADS = (4 + TC_PW + 1) * 32;
 constexpr int TC_MAX_K = 32;
 constexpr int TC_STG_COLS = 128;               // epilogue staging width (columns)
+constexpr int TC_SCHED = 4;                    // launch-control responses in flight (ring)
 constexpr uint32_t TC_TMEM_COLS = 512;
 
 struct TcParams {
@@ -67,6 +68,7 @@ struct TcParams {
     int n_buf;    // TMEM accumulator buffers (2 when tile_n <= 256)
     int grid_y;   // column tiles per row tile
     int64_t n_tiles;
+    int dynamic;  // 1: one CTA per tile, CTAs claim unlaunched tiles by cluster launch control
     int stg_cols; // epilogue staging width: a multiple of 32 dividing tile_n, <= TC_STG_COLS
     // epilogue
     const __nv_bfloat16* residual;
@@ -187,13 +189,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint8_t* b_smem = a_smem + S * TC_A_BYTES;
     uint8_t* stg_smem = b_smem + S * B_BYTES;                                    // 4 warps
     int32_t* nbr_s = reinterpret_cast<int32_t*>(stg_smem + 4 * 32 * (stg_units + 1) * 16);  // [TC_BM][K]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(nbr_s + TC_BM * K);
+    uint4* sched_resp = reinterpret_cast<uint4*>(nbr_s + TC_BM * K);  // [TC_SCHED] launch-control responses
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sched_resp + TC_SCHED);
     uint64_t* full = bars;                 // [S] MMA may read the stage (leader / single CTA)
     uint64_t* afull = bars + S;            // [S] PAIR peer: this CTA's A copies have landed
     uint64_t* empty = bars + 2 * S;        // [S] the MMAs reading the stage are done
     uint64_t* tmem_full = bars + 3 * S;    // [2]
     uint64_t* tmem_empty = bars + 3 * S + 2;
-    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);  // [S] PAIR relay: last step of a tile
+    uint64_t* sched_full = bars + 3 * S + 4;               // [TC_SCHED] response landed
+    uint64_t* sched_empty = sched_full + TC_SCHED;         // [TC_SCHED] every role has read it
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(sched_empty + TC_SCHED);  // [S] PAIR relay: last step of a tile
     uint32_t* tile_steps = stage_flags + S;  // [8] reduction steps per tile, ring over tiles
     // (the producers run at most S <= 8 stages, so at most 8 one-step tiles, ahead of the MMA thread)
     uint32_t* misc = tile_steps + 8;      // [0] tmem base, [1] abort
@@ -206,6 +211,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int64_t n_units = PAIR ? (int64_t)(gridDim.x >> 1) : (int64_t)gridDim.x;
     constexpr int TILE_ROWS = PAIR ? 2 * TC_BM : TC_BM;
     const int64_t my_tiles = p.n_tiles > unit ? (p.n_tiles - 1 - unit) / n_units + 1 : 0;
+    const bool dyn = !PAIR && p.dynamic != 0;
+    // Tile sequence of this CTA.  Static: unit, unit + n_units, ...  Dynamic:
+    // its own tile, then one tile per successful launch-control response.
+    // Tile ids run backwards from the launch order so that the last row
+    // tiles (the fullest tap masks when rows are mask-sorted) start first.
+    const int64_t first_tile = dyn ? p.n_tiles - 1 - (int64_t)blockIdx.x : (my_tiles > 0 ? unit : -1);
+    // next tile after local tile lt, or -1; `arrive` makes this caller's read
+    // of response lt count towards the slot's release
+    auto next_tile = [&](int64_t lt, bool arrive) -> int64_t {
+        if (!dyn) return lt + 1 < my_tiles ? unit + (lt + 1) * n_units : -1;
+        const int q = (int)(lt % TC_SCHED);
+        if (!mbar_wait(&sched_full[q], (uint32_t)((lt / TC_SCHED) & 1))) return -2;
+        const int64_t x = clc_cancelled_x(&sched_resp[q]);
+        if (arrive) mbar_arrive(&sched_empty[q]);
+        return x < 0 ? -1 : p.n_tiles - 1 - x;
+    };
     const int n_chunks = (p.cin + TC_BK - 1) / TC_BK;
     constexpr int MMA_WARP = 4 + TC_PW;
 
@@ -219,6 +240,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);            // tcgen05.commit after a tile's last MMA
             mbar_init(&tmem_empty[b], PAIR ? 8 : 4);  // one arrive per epilogue warp (of both CTAs)
+        }
+        for (int q = 0; q < TC_SCHED; ++q) {
+            mbar_init(&sched_full[q], 1);           // the requester's expect_tx arrive
+            mbar_init(&sched_empty[q], TC_PW + 1 + 4);  // producer warps, MMA thread, epilogue warps
         }
         misc[1] = 0;
         fence_mbar_init();
@@ -255,8 +280,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         int s = 0;          // stage ring position and its phase bit
         uint32_t ph = 0;
         bool ok = true;
-        for (int64_t lt = 0; lt < my_tiles && ok; ++lt) {
-            const int64_t tile = unit + lt * n_units;
+        int64_t tile = first_tile;
+        int64_t requested = 0;  // launch-control requests issued (producer warp 0)
+        for (int64_t lt = 0; tile >= 0 && ok; ++lt) {
+            if (dyn && pw == 0) {
+                // ask for the tile after this one; its response is read when this tile's stages are issued
+                bool got = true;
+                if (lane == 0) {
+                    const int q = (int)(lt % TC_SCHED);
+                    got = mbar_wait(&sched_empty[q], (uint32_t)(((lt / TC_SCHED) & 1) ^ 1));
+                    if (got) {
+                        fence_proxy_async_smem();  // earlier generic reads of the slot before the async write
+                        mbar_arrive_expect_tx(&sched_full[q], 16u);
+                        clc_try_cancel(&sched_resp[q], &sched_full[q]);
+                        requested = lt + 1;
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, got, 0)) {
+                    ok = false;
+                    break;
+                }
+            }
             const int64_t tile_row0 = (tile / p.grid_y) * TILE_ROWS;
             const int n0 = (int)(tile % p.grid_y) * p.tile_n;
             // neighbor rows of the whole tile (the common tap mask), mine kept in smem
@@ -377,6 +421,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
             }
+            if (!ok) break;
+            int64_t nt = 0;
+            if (lane == 0) nt = next_tile(lt, true);
+            nt = __shfl_sync(0xffffffffu, nt, 0);
+            if (nt == -2) ok = false;
+            tile = nt;
+        }
+        if (dyn && pw == 0 && lane == 0 && !ok && requested > 0) {
+            // a request whose response nobody read: let it land before the CTA exits
+            const int64_t q = requested - 1;
+            mbar_wait(&sched_full[q % TC_SCHED], (uint32_t)((q / TC_SCHED) & 1));
         }
         cp_async_wait<0>();
         if (!ok) *abort_flag = 1u;
@@ -413,7 +468,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int64_t lt = 0; lt < my_tiles && ok; ++lt) {
+            int64_t tile = first_tile;
+            for (int64_t lt = 0; tile >= 0 && ok; ++lt) {
                 const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
                 const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
                 if (!mbar_wait(&tmem_empty[b], (use & 1u) ^ 1u)) {
@@ -459,6 +515,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     umma_commit_pair(&tmem_full[b], 0x3);
                 else
                     umma_commit(&tmem_full[b]);
+                tile = next_tile(lt, true);
+                if (tile == -2) ok = false;
             }
             if (!ok) *abort_flag = 1u;
         }
@@ -472,8 +530,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const bool multi = p.ln != 0 || p.out2 != nullptr;
         const bool dense_res = p.residual != nullptr && p.res_off == nullptr;
         const uint32_t leader_tmem_empty = PAIR ? mapa_shared(smem_u32(tmem_empty), 0) : 0u;
-        for (int64_t lt = 0; lt < my_tiles; ++lt) {
-            const int64_t tile = unit + lt * n_units;
+        int64_t tile = first_tile;
+        for (int64_t lt = 0; tile >= 0; ++lt) {
             const int64_t tile_base = (tile / p.grid_y) * TILE_ROWS + (int64_t)rank * TC_BM;
             const int n0 = (int)(tile % p.grid_y) * p.tile_n;
             const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
@@ -648,6 +706,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 else
                     mbar_arrive(&tmem_empty[b]);
             }
+            int64_t nt = 0;
+            if (lane == 0) nt = next_tile(lt, true);
+            tile = __shfl_sync(0xffffffffu, nt, 0);
+            if (tile == -2) {
+                *abort_flag = 1u;
+                break;
+            }
         }
     }
 
@@ -677,7 +742,7 @@ inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair) {
     const int stg_cols = tc_stg_cols(tile_n);
     const size_t b_bytes = (size_t)(pair ? tile_n / 2 : tile_n) * 128;
     return 1024 + (size_t)stages * (TC_A_BYTES + b_bytes) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
-           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16;
+           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16);
 }
 
 }  // namespace sc

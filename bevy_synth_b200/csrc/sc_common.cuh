@@ -113,20 +113,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// try_wait with a suspend-time hint: the thread sleeps until the phase
-// completes or about `ns` nanoseconds pass, instead of re-polling.
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
-        : "memory");
-    return ok != 0;
-}
-
 // Bounded wait: returns false (and raises FAULT_WAIT_TIMEOUT) if the phase
 // with `parity` has not completed within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
@@ -139,6 +125,43 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
             return false;
         }
     }
+}
+
+// ---- cluster launch control (sm_100): dynamic tile scheduling ------------
+// try_cancel asks the hardware to cancel the launch of a CTA of this grid
+// that has not started yet; the 16-byte response lands in shared memory and
+// completes 16 bytes of transaction on `bar`.  A successful response names
+// the cancelled CTA, whose work the caller then does itself.
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+    asm volatile(
+        "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+            smem_u32(resp)),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Decodes a response: the x index of the cancelled CTA, or -1 when the
+// request failed (every CTA of the grid has started or been cancelled).
+__device__ __forceinline__ int64_t clc_cancelled_x(const void* resp) {
+    ulonglong2 r;
+    asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(r.x), "=l"(r.y) : "r"(smem_u32(resp)) : "memory");
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+        "mov.b128 r, {%1, %2};\n\t"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "l"(r.x), "l"(r.y));
+    if (!ok) return -1;
+    uint32_t x;
+    asm volatile(
+        "{\n\t.reg .b128 r;\n\t"
+        "mov.b128 r, {%1, %2};\n\t"
+        "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, r;\n\t}"
+        : "=r"(x)
+        : "l"(r.x), "l"(r.y));
+    return (int64_t)x;
 }
 
 // ------------------------------------------------------------ cp.async --

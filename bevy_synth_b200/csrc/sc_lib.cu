@@ -107,6 +107,14 @@ struct TcPlan {
 
 // The CTA-pair (2-SM) kernel is opt-in (SC_TC_PAIR=1) until it is the faster
 // one on the measured workloads; the single-CTA kernel is the default.
+static bool use_static_schedule() {
+    static const bool v = [] {
+        const char* e = std::getenv("SC_TC_STATIC");
+        return e && e[0] == '1';
+    }();
+    return v;
+}
+
 static bool allow_pair() {
     const char* e = std::getenv("SC_TC_PAIR");
     return e && e[0] == '1';
@@ -232,7 +240,12 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     });
     SC_CUDA_TRY(attr_err);
     if (!plan.pair) {
-        const int64_t ctas = std::min<int64_t>(p.n_tiles, sm_count());
+        // Default: one CTA per tile; a running CTA claims tiles of CTAs that
+        // have not started (cluster launch control), so tiles are balanced
+        // dynamically.  SC_TC_STATIC=1: a persistent grid with round-robin tiles.
+        p.dynamic = use_static_schedule() ? 0 : 1;
+        const int64_t ctas = p.dynamic ? p.n_tiles : std::min<int64_t>(p.n_tiles, sm_count());
+        if (ctas > 0x7fffffff) return fail(SC_ERR_UNSUPPORTED, "too many row tiles for one launch");
         conv_tc_kernel<false><<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, p);
     } else {
         cudaLaunchConfig_t lc;
