@@ -45,7 +45,7 @@ namespace sc {
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;                      // channels per reduction step
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
-constexpr int TC_PW = 2;                       // gather producer warps
+constexpr int TC_PW = 2;                       // gather producer warps (the tap-mask exchange assumes 2)
 constexpr int TC_THREADS = (4 + TC_PW + 1) * 32;
 constexpr int TC_MAX_K = 32;
 constexpr int TC_STG_COLS = 128;               // epilogue staging width (columns)
@@ -198,10 +198,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t* tmem_empty = bars + 3 * S + 2;
     uint64_t* sched_full = bars + 3 * S + 4;               // [TC_SCHED] response landed
     uint64_t* sched_empty = sched_full + TC_SCHED;         // [TC_SCHED] every role has read it
-    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(sched_empty + TC_SCHED);  // [S] PAIR relay: last step of a tile
+    uint64_t* mask_bar = sched_empty + TC_SCHED;           // both producer warps posted their tap mask
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(mask_bar + 1);  // [S] PAIR relay: last step of a tile
     uint32_t* tile_steps = stage_flags + S;  // [8] reduction steps per tile, ring over tiles
     // (the producers run at most S <= 8 stages, so at most 8 one-step tiles, ahead of the MMA thread)
     uint32_t* misc = tile_steps + 8;      // [0] tmem base, [1] abort
+    uint32_t* mask_s = misc + 4;          // [2][TC_PW] tap masks per producer warp, by tile parity
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -245,6 +247,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&sched_full[q], 1);           // the requester's expect_tx arrive
             mbar_init(&sched_empty[q], TC_PW + 1 + 4);  // producer warps, MMA thread, epilogue warps
         }
+        mbar_init(mask_bar, TC_PW);
         misc[1] = 0;
         fence_mbar_init();
         fence_proxy_async_smem();
@@ -282,6 +285,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         bool ok = true;
         int64_t tile = first_tile;
         int64_t requested = 0;  // launch-control requests issued (producer warp 0)
+        // Contiguous map rows (no row order, or a pre-ordered map) on one CTA:
+        // each producer warp reads only its own rows' map block, one tile
+        // ahead, into registers (16-byte loads, all in flight at once), and
+        // the two warps OR their tap masks through mask_bar.
+        const bool fast_map = !PAIR && (p.row_order == nullptr || p.nbr_ordered != nullptr);
+        const int32_t* map_rows = p.nbr_ordered ? p.nbr_ordered : p.nbr;
+        constexpr int QV = (ROWS * TC_MAX_K / 4 + 31) / 32;  // int4 per lane for ROWS rows of <= 32 taps
+        const int my_vec = ROWS * K / 4;                       // int4 of my rows' block (K * 64 / 4)
+        int4 qmap[QV];
+        auto load_my_map = [&](int64_t t_next) {
+            const int64_t r0 = (t_next / p.grid_y) * TILE_ROWS + pw * ROWS;
+            const int64_t left = p.n_rows - r0;
+            const int n_my = left <= 0 ? 0 : (left < ROWS ? (int)left : ROWS);
+            const int n_int = n_my * K;
+            const int32_t* blk = map_rows + r0 * K;
+#pragma unroll
+            for (int u = 0; u < QV; ++u) {
+                const int f4 = u * 32 + lane;
+                if (4 * f4 + 3 < n_int) {
+                    qmap[u] = __ldg(reinterpret_cast<const int4*>(blk) + f4);
+                } else {
+                    qmap[u].x = 4 * f4 < n_int ? __ldg(blk + 4 * f4) : -1;
+                    qmap[u].y = 4 * f4 + 1 < n_int ? __ldg(blk + 4 * f4 + 1) : -1;
+                    qmap[u].z = 4 * f4 + 2 < n_int ? __ldg(blk + 4 * f4 + 2) : -1;
+                    qmap[u].w = -1;
+                }
+            }
+        };
+        if (fast_map && tile >= 0) load_my_map(tile);
         for (int64_t lt = 0; tile >= 0 && ok; ++lt) {
             if (dyn && pw == 0) {
                 // ask for the tile after this one; its response is read when this tile's stages are issued
@@ -308,7 +340,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int64_t n_valid = p.n_rows - tile_row0 < TILE_ROWS ? p.n_rows - tile_row0 : TILE_ROWS;
             const int n_ints = (int)n_valid * K;
             const uint64_t kdiv = (1ull << 32) / (uint64_t)K + 1ull;  // f / K == (f * kdiv) >> 32 here
-            if (p.row_order == nullptr || p.nbr_ordered != nullptr) {
+            if (fast_map) {
+                // my rows' map block (prefetched) -> my_nbr, checked; this warp's tap mask
+#pragma unroll
+                for (int u = 0; u < QV; ++u) {
+                    const int f4 = u * 32 + lane;
+                    if (f4 < my_vec) {
+                        int32_t v[4] = {qmap[u].x, qmap[u].y, qmap[u].z, qmap[u].w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            if (v[e] < -1 || v[e] >= p.n_in) {
+                                raise_fault(FAULT_BAD_NEIGHBOR);
+                                v[e] = -1;
+                            }
+                            if (v[e] >= 0) {
+                                const int f = 4 * f4 + e;
+                                mask |= 1u << (f - (int)(((uint64_t)f * kdiv) >> 32) * K);
+                            }
+                        }
+                        reinterpret_cast<int4*>(my_nbr)[f4] = make_int4(v[0], v[1], v[2], v[3]);
+                    }
+                }
+            } else if (p.row_order == nullptr || p.nbr_ordered != nullptr) {
                 // the tile's map rows are contiguous: independent 16-byte loads,
                 // issued 8 deep before any is consumed (one latency per batch)
                 const int32_t* blk = (p.nbr_ordered ? p.nbr_ordered : p.nbr) + tile_row0 * K;
@@ -371,15 +424,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
             }
             mask = __reduce_or_sync(0xffffffffu, mask);
+            {
+                // OR of both producer warps' masks (equal on the other paths, which read every row)
+                bool got = true;
+                if (lane == 0) {
+                    mask_s[2 * (lt & 1) + pw] = mask;
+                    mbar_arrive(mask_bar);
+                    got = mbar_wait(mask_bar, (uint32_t)(lt & 1));
+                    if (got) mask = mask_s[2 * (lt & 1)] | mask_s[2 * (lt & 1) + 1];
+                }
+                if (!__shfl_sync(0xffffffffu, got, 0)) {
+                    ok = false;
+                    break;
+                }
+                mask = __shfl_sync(0xffffffffu, mask, 0);
+            }
             if (mask == 0) mask = 1;  // a tile with no valid tap still runs one (all-zero) step
             __syncwarp();
             const int n_steps = __popc(mask) * n_chunks;
             int step = 0;
+            int64_t nt = -1;
             for (uint32_t m = mask; m && ok; m &= m - 1) {
                 const int k = __ffs(m) - 1;
                 int32_t src[GROUPS];
 #pragma unroll
                 for (int i = 0; i < GROUPS; ++i) src[i] = my_nbr[(i * 4 + sub) * K + k];
+                if ((m & (m - 1)) == 0) {
+                    // last tap: learn the next tile and start loading its map rows
+                    if (lane == 0) nt = next_tile(lt, true);
+                    nt = __shfl_sync(0xffffffffu, nt, 0);
+                    if (nt == -2) {
+                        ok = false;
+                        break;
+                    }
+                    if (fast_map && nt >= 0) load_my_map(nt);
+                }
                 for (int ch = 0; ch < n_chunks; ++ch, ++step) {
                     if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u))) {
                         ok = false;
@@ -422,10 +501,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
             }
             if (!ok) break;
-            int64_t nt = 0;
-            if (lane == 0) nt = next_tile(lt, true);
-            nt = __shfl_sync(0xffffffffu, nt, 0);
-            if (nt == -2) ok = false;
             tile = nt;
         }
         if (dyn && pw == 0 && lane == 0 && !ok && requested > 0) {
@@ -458,10 +533,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (flags & 2u) ++lt;
                 }
             }
-        } else if (lane == 0) {
+        } else {
             // ================================================ MMA issuer
-            // The tensor pipe's queue is short: this loop is kept to wait,
-            // fence, four MMAs and a commit per stage.
+            // The whole warp runs the loop (waits, descriptors and tile
+            // bookkeeping stay warp-uniform) and one elected lane issues the
+            // MMAs and their commits: issued from single-lane divergent code
+            // the same MMAs kept the tensor pipe idle ~40% of the time.
+            const bool issuer = elect_one();
+            const int issuer_lane = __ffs(__ballot_sync(0xffffffffu, issuer)) - 1;
             const uint32_t idesc = PAIR ? umma_idesc_bf16_m256((uint32_t)p.sub_n) : umma_idesc_bf16_m128((uint32_t)p.sub_n);
             const uint64_t adesc0 = umma_desc_sw128(smem_u32(a_smem));
             const uint64_t bdesc0 = umma_desc_sw128(smem_u32(b_smem));
@@ -472,7 +551,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int64_t lt = 0; tile >= 0 && ok; ++lt) {
                 const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
                 const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
-                if (!mbar_wait(&tmem_empty[b], (use & 1u) ^ 1u)) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&tmem_empty[b], (use & 1u) ^ 1u))) {
                     ok = false;
                     break;
                 }
@@ -480,7 +559,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const uint32_t acc = tmem_base + (uint32_t)(b * 256);
                 uint32_t steps = 0;
                 for (uint32_t step = 0;; ++step) {
-                    if (!mbar_wait(&full[s], ph)) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph))) {
                         ok = false;
                         break;
                     }
@@ -489,21 +568,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (step == 0) steps = tile_steps[lt & 7];
                     const uint64_t ad = adesc0 + (uint64_t)((s * TC_A_BYTES) >> 4);
                     const uint64_t bd = bdesc0 + (uint64_t)((s * B_BYTES) >> 4);
+                    if (issuer) {
 #pragma unroll
-                    for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                        for (int q = 0; q < p.n_sub; ++q) {
-                            const uint64_t bq = bd + (uint64_t)((q * B_ROWS * 128 + kk * 32) >> 4);
+                        for (int kk = 0; kk < TC_BK / 16; ++kk) {
                             const uint32_t accum = (step == 0 && kk == 0) ? 0u : 1u;
-                            if (PAIR)
-                                umma_bf16_pair(acc + q * p.sub_n, ad + (uint64_t)(kk * 2), bq, idesc, accum);
-                            else
-                                umma_bf16(acc + q * p.sub_n, ad + (uint64_t)(kk * 2), bq, idesc, accum);
+                            // K step kk: +32 bytes inside the 128-byte swizzled rows
+                            if (PAIR) {
+                                umma_bf16_pair(acc, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, accum);
+                                if (p.n_sub == 2)
+                                    umma_bf16_pair(acc + p.sub_n, ad + (uint64_t)(kk * 2),
+                                                   bd + (uint64_t)((B_ROWS * 128 + kk * 32) >> 4), idesc, accum);
+                            } else {
+                                umma_bf16(acc, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc, accum);
+                                if (p.n_sub == 2)
+                                    umma_bf16(acc + p.sub_n, ad + (uint64_t)(kk * 2),
+                                              bd + (uint64_t)((B_ROWS * 128 + kk * 32) >> 4), idesc, accum);
+                            }
                         }
+                        if (PAIR)
+                            umma_commit_pair(&empty[s], 0x3);
+                        else
+                            umma_commit(&empty[s]);
                     }
-                    if (PAIR)
-                        umma_commit_pair(&empty[s], 0x3);
-                    else
-                        umma_commit(&empty[s]);
+                    __syncwarp();
                     if (++s == S) {
                         s = 0;
                         ph ^= 1u;
@@ -511,14 +598,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (step + 1 >= steps) break;
                 }
                 if (!ok) break;
-                if (PAIR)
-                    umma_commit_pair(&tmem_full[b], 0x3);
-                else
-                    umma_commit(&tmem_full[b]);
-                tile = next_tile(lt, true);
+                if (issuer) {
+                    if (PAIR)
+                        umma_commit_pair(&tmem_full[b], 0x3);
+                    else
+                        umma_commit(&tmem_full[b]);
+                }
+                __syncwarp();
+                int64_t nt = 0;
+                if (issuer) nt = next_tile(lt, true);
+                tile = __shfl_sync(0xffffffffu, nt, issuer_lane);
                 if (tile == -2) ok = false;
             }
-            if (!ok) *abort_flag = 1u;
+            if (!ok && issuer) *abort_flag = 1u;
         }
     } else {
         // ====================================================== epilogue
@@ -729,20 +821,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }
 
 // Epilogue staging width: the largest multiple of 32 that divides tile_n
-// and is at most TC_STG_COLS, so staging groups tile the row exactly.
-inline int tc_stg_cols(int tile_n) {
-    for (int c = TC_STG_COLS; c >= 32; c -= 32)
+// and is at most `cap` (<= TC_STG_COLS), so staging groups tile the row exactly.
+inline int tc_stg_cols(int tile_n, int cap = TC_STG_COLS) {
+    for (int c = cap; c >= 32; c -= 32)
         if (tile_n % c == 0) return c;
     return 32;
 }
 
 // Dynamic shared-memory bytes of a launch (1 KB alignment slack included);
 // with `pair`, a CTA holds half of the B rows.
-inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair) {
-    const int stg_cols = tc_stg_cols(tile_n);
+inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair, int stg_cols) {
     const size_t b_bytes = (size_t)(pair ? tile_n / 2 : tile_n) * 128;
     return 1024 + (size_t)stages * (TC_A_BYTES + b_bytes) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
-           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16);
+           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 16;
 }
 
 }  // namespace sc

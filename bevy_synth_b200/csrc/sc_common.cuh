@@ -127,6 +127,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// One lane of the (fully active) warp, the same lane on every call.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // ---- cluster launch control (sm_100): dynamic tile scheduling ------------
 // try_cancel asks the hardware to cancel the launch of a CTA of this grid
 // that has not started yet; the 16-byte response lands in shared memory and

@@ -100,7 +100,7 @@ static bool force_simt() {
 }
 
 struct TcPlan {
-    int tile_n, n_sub, sub_n, stages, grid_y, n_buf;
+    int tile_n, n_sub, sub_n, stages, grid_y, n_buf, stg_cols;
     bool pair;  // 2-SM (cta_group::2) kernel on CTA pairs
     size_t smem;
 };
@@ -163,15 +163,35 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     plan->n_buf = tile_n <= 256 ? 2 : 1;
     plan->grid_y = (int)(cout / tile_n);
     plan->pair = allow_pair() && plan->sub_n >= 32;
-    int S = 8;
-    while (S >= 2 && tc_smem_bytes(S, tile_n, (int)K, plan->pair) > kMaxDynSmem) --S;
+    // Deepest stage ring that fits; a narrower epilogue staging buffer is
+    // taken when it buys a stage (SC_TC_STG=64|128 pins the width).
+    auto deepest = [&](int stg) {
+        int S = 8;
+        while (S >= 2 && tc_smem_bytes(S, tile_n, (int)K, plan->pair, stg) > kMaxDynSmem) --S;
+        return S;
+    };
+    int stg = tc_stg_cols(tile_n, 128);
+    int S = deepest(stg);
+    const char* stg_env = std::getenv("SC_TC_STG");
+    if (stg_env && std::atoi(stg_env) == 64) {
+        stg = tc_stg_cols(tile_n, 64);
+        S = deepest(stg);
+    } else if (!stg_env) {
+        const int stg64 = tc_stg_cols(tile_n, 64);
+        const int s64 = deepest(stg64);
+        if (s64 > S) {
+            stg = stg64;
+            S = s64;
+        }
+    }
     if (const char* env = std::getenv("SC_TC_STAGES")) {  // tuning override, clamped to what fits
         const int want = std::atoi(env);
         if (want >= 2 && want < S) S = want;
     }
     if (S < 2) return false;
     plan->stages = S;
-    plan->smem = tc_smem_bytes(S, tile_n, (int)K, plan->pair);
+    plan->stg_cols = stg;
+    plan->smem = tc_smem_bytes(S, tile_n, (int)K, plan->pair, stg);
     return true;
 }
 
@@ -210,7 +230,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     p.grid_y = plan.grid_y;
     const int64_t tile_rows = plan.pair ? 2 * TC_BM : TC_BM;
     p.n_tiles = ((n_rows + tile_rows - 1) / tile_rows) * plan.grid_y;
-    p.stg_cols = tc_stg_cols(plan.tile_n);
+    p.stg_cols = plan.stg_cols;
     if (p.stg_cols % 32 != 0 || plan.tile_n % p.stg_cols != 0)
         return fail(SC_ERR_UNSUPPORTED, "internal: staging width does not tile the output tile");
     p.residual = static_cast<const __nv_bfloat16*>(e.d_residual);
@@ -570,8 +590,10 @@ int sc_subm_conv_forward(const sc_conv_config* cfg, sc_dtype dtype, const void* 
         return fail(SC_ERR_INVALID, "residual_repeat must be >= 1");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     TcPlan plan;
+    // the tensor-core kernel reads the map, bias and LayerNorm parameters in 16-byte vectors
     const bool al = aligned16(in) && aligned16(w) && aligned16(out) && aligned16(e.d_out2) &&
-                    aligned16(e.d_residual);
+                    aligned16(e.d_residual) && aligned16(nbr) && aligned16(e.d_neighbor_rows_ordered) &&
+                    aligned16(bias) && aligned16(e.d_ln_gamma) && aligned16(e.d_ln_beta);
     if (al && plan_tc(cfg, dtype, e, &plan))
         return launch_tc(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st, plan);
     if (dtype == SC_DTYPE_F32) return launch_simt<float>(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st);
