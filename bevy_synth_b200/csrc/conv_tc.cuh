@@ -17,21 +17,29 @@
 //   * tcgen05.mma (M=128, N<=256 per instruction, K=16) accumulates in fp32
 //     TMEM; taps that are invalid for every row of a tile are skipped.
 //
-// Persistent, warp-specialised CTA (one per SM, static round-robin tiles):
+// Warp-specialised CTA, one per SM.  The single-CTA kernel is launched with
+// one CTA per tile; a running CTA claims the tiles of CTAs that have not
+// started (cluster launch control), so tiles spread dynamically, largest
+// first.  Roles:
 //   warps 0-3          epilogue: thread i owns TMEM lane / tile row i; output
 //                      and residual rows move through padded smem staging so
 //                      that global accesses are whole coalesced rows;
-//   warps 4..4+PW-1    A gather producers; warp 4 lane 0 also issues the
-//                      weight TMA and tags each stage first/last of its tile;
-//   warp 4+PW          MMA issuer (one thread).
+//   warps 4..4+PW-1    A gather producers, one per SM sub-partition; each
+//                      reads its rows' map block one tile ahead; warp 4 lane 0
+//                      also issues the weight TMA and the launch-control
+//                      requests;
+//   warp 4+PW          MMA warp: the whole warp runs the loop, one elected
+//                      lane issues tcgen05.mma and the commits.
+// Optionally (SC_TC_GATHER4=1) A rows arrive by TMA tile::gather4 instead of
+// cp.async; on B200 that measured slower for 128-byte rows.
 // The accumulator is double-buffered in TMEM (2 x 256 columns) when
 // tile_n <= 256, so the epilogue of one tile overlaps the MMAs of the next.
 //
-// PAIR (2-SM) variant, launched as clusters of two CTAs: a tile is 256 rows,
+// PAIR (2-SM) variant (opt-in, SC_TC_PAIR=1; persistent grid with static
+// round-robin tiles), launched as clusters of two CTAs: a tile is 256 rows,
 // 128 per CTA; the leader issues tcgen05.mma.cta_group::2 with M = 256, each
 // CTA's A from its own shared memory and B split by N across the pair, so a
-// CTA loads and the tensor cores read only half of every weight tile (the
-// single-CTA kernel's shared-memory traffic is its limit).  Both halves of B
+// CTA loads and the tensor cores read only half of every weight tile.  Both halves of B
 // arrive by TMA on the leader's full barrier; the peer's "A landed" is relayed
 // by its otherwise idle MMA warp; commits are multicast to both CTAs.
 // Every mbarrier wait is bounded: on expiry the device fault word is raised
@@ -45,7 +53,14 @@ namespace sc {
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;                      // channels per reduction step
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
-constexpr int TC_PW = 2;                       // gather producer warps (the tap-mask exchange assumes 2)
+#ifndef SC_TC_PW
+#define SC_TC_PW 4
+#endif
+// Gather producer warps.  One per SM sub-partition: the cp.async issue queue
+// is per sub-partition, and with two warps it, not the tensor pipe, set the
+// stage rate.
+constexpr int TC_PW = SC_TC_PW;
+static_assert(TC_PW == 2 || TC_PW == 4 || TC_PW == 8, "producer warps");
 constexpr int TC_THREADS = (4 + TC_PW + 1) * 32;
 constexpr int TC_MAX_K = 32;
 constexpr int TC_STG_COLS = 128;               // epilogue staging width (columns)
@@ -69,6 +84,7 @@ struct TcParams {
     int grid_y;   // column tiles per row tile
     int64_t n_tiles;
     int dynamic;  // 1: one CTA per tile, CTAs claim unlaunched tiles by cluster launch control
+    int gather4;  // 1: A rows gathered by TMA (tile::gather4 on `amap`) instead of cp.async
     int stg_cols; // epilogue staging width: a multiple of 32 dividing tile_n, <= TC_STG_COLS
     // epilogue
     const __nv_bfloat16* residual;
@@ -174,7 +190,8 @@ __device__ __forceinline__ void add_param32(float (&v)[32], const float* p, bool
 
 template <bool PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcParams p) {
+    conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
+                   const TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -234,8 +251,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            // gather lanes (async, .noinc) + the producer's expect_tx arrive (+ the peer's relay)
-            mbar_init(&full[s], TC_PW * 32 + 1 + (PAIR ? 1 : 0));
+            // gather lanes (async, .noinc) + the producer's expect_tx arrive (+ the peer's relay);
+            // with TMA gathers one expect_tx arrive per producer warp
+            mbar_init(&full[s], (!PAIR && p.gather4) ? TC_PW : TC_PW * 32 + 1 + (PAIR ? 1 : 0));
             mbar_init(&afull[s], TC_PW * 32 + 1);   // PAIR peer: gather lanes + the flags arrive
             mbar_init(&empty[s], 1);                // one tcgen05.commit
         }
@@ -290,6 +308,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ahead, into registers (16-byte loads, all in flight at once), and
         // the two warps OR their tap masks through mask_bar.
         const bool fast_map = !PAIR && (p.row_order == nullptr || p.nbr_ordered != nullptr);
+        const bool G4 = !PAIR && p.gather4 != 0;
         const int32_t* map_rows = p.nbr_ordered ? p.nbr_ordered : p.nbr;
         constexpr int QV = (ROWS * TC_MAX_K / 4 + 31) / 32;  // int4 per lane for ROWS rows of <= 32 taps
         const int my_vec = ROWS * K / 4;                       // int4 of my rows' block (K * 64 / 4)
@@ -428,10 +447,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 // OR of both producer warps' masks (equal on the other paths, which read every row)
                 bool got = true;
                 if (lane == 0) {
-                    mask_s[2 * (lt & 1) + pw] = mask;
+                    mask_s[TC_PW * (lt & 1) + pw] = mask;
                     mbar_arrive(mask_bar);
                     got = mbar_wait(mask_bar, (uint32_t)(lt & 1));
-                    if (got) mask = mask_s[2 * (lt & 1)] | mask_s[2 * (lt & 1) + 1];
+                    if (got) {
+                        mask = 0;
+#pragma unroll
+                        for (int w = 0; w < TC_PW; ++w) mask |= mask_s[TC_PW * (lt & 1) + w];
+                    }
                 }
                 if (!__shfl_sync(0xffffffffu, got, 0)) {
                     ok = false;
@@ -447,8 +470,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (uint32_t m = mask; m && ok; m &= m - 1) {
                 const int k = __ffs(m) - 1;
                 int32_t src[GROUPS];
+                if (G4) {
+                    // lanes below ROWS/4: the four rows 4*lane .. 4*lane+3 of my rows (absent rows read as zeros)
 #pragma unroll
-                for (int i = 0; i < GROUPS; ++i) src[i] = my_nbr[(i * 4 + sub) * K + k];
+                    for (int e = 0; e < 4; ++e) {
+                        const int32_t v = lane < ROWS / 4 ? my_nbr[(4 * lane + e) * K + k] : -1;
+                        src[e] = v >= 0 ? v : (int32_t)p.n_in;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < GROUPS; ++i) src[i] = my_nbr[(i * 4 + sub) * K + k];
+                }
                 if ((m & (m - 1)) == 0) {
                     // last tap: learn the next tile and start loading its map rows
                     if (lane == 0) nt = next_tile(lt, true);
@@ -463,6 +495,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u))) {
                         ok = false;
                         break;
+                    }
+                    if (G4) {
+                        // A by TMA row gathers: each warp posts its bytes, then lanes 0-15 issue
+                        const uint32_t stage = smem_u32(a_smem + s * TC_A_BYTES);
+                        if (lane == 0) {
+                            if (pw == 0) {
+                                if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
+                                stage_flags[s] = step == n_steps - 1 ? 2u : 0u;
+                            }
+                            mbar_arrive_expect_tx(&full[s], (uint32_t)(TC_A_BYTES / TC_PW + (pw == 0 ? B_BYTES : 0)));
+                            if (pw == 0) {
+                                const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
+                                for (int q = 0; q < p.n_sub; ++q)
+                                    tma_load_3d(dst + q * B_ROWS * 128, &wmap, &full[s], ch * TC_BK, k,
+                                                n0 + q * p.sub_n);
+                            }
+                        }
+                        __syncwarp();
+                        if (lane < ROWS / 4)
+                            tma_gather4(stage + (uint32_t)((pw * ROWS + 4 * lane) * 128), &amap, &full[s], ch * TC_BK,
+                                        src[0], src[1], src[2], src[3]);
+                        if (++s == S) {
+                            s = 0;
+                            ph ^= 1u;
+                        }
+                        continue;
                     }
                     if (pw == 0 && lane == 0) {
                         // published to the MMA thread by this stage's full-barrier arrive below
@@ -833,7 +891,7 @@ inline int tc_stg_cols(int tile_n, int cap = TC_STG_COLS) {
 inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair, int stg_cols) {
     const size_t b_bytes = (size_t)(pair ? tile_n / 2 : tile_n) * 128;
     return 1024 + (size_t)stages * (TC_A_BYTES + b_bytes) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
-           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 16;
+           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 8 * TC_PW;
 }
 
 }  // namespace sc

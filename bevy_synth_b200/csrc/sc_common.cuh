@@ -208,6 +208,18 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* desc, uint
         : "memory");
 }
 
+// Row gather: four rows (y0..y3) of a 2-D tensor map, `box_x` columns from
+// x, land as four consecutive box rows at dst (the map's swizzle applied).
+// Rows outside the tensor read as zeros.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* desc, uint64_t* bar, int x, int y0, int y1,
+                                            int y2, int y3) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cta.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+        "l"(desc), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
+        : "memory");
+}
+
 // ------------------------------------------------------- clusters (2-SM) --
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

@@ -115,6 +115,14 @@ static bool use_static_schedule() {
     return v;
 }
 
+static bool use_gather4() {
+    static const bool v = [] {
+        const char* e = std::getenv("SC_TC_GATHER4");
+        return e && e[0] == '1';
+    }();
+    return v;
+}
+
 static bool allow_pair() {
     const char* e = std::getenv("SC_TC_PAIR");
     return e && e[0] == '1';
@@ -212,8 +220,25 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     if (r != CUDA_SUCCESS)
         return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
 
+    // A rows by TMA gather (tile::gather4): the features as a 2-D map [n_in, cin], 64-column boxes
+    CUtensorMap amap;
+    memset(&amap, 0, sizeof amap);
+    const bool g4 = !plan.pair && use_gather4() && cin % 8 == 0 && n_in > 0 && n_in < 0x7fffffff;
+    if (g4) {
+        cuuint64_t adims[2] = {(cuuint64_t)cin, (cuuint64_t)n_in};
+        cuuint64_t astr[1] = {(cuuint64_t)cin * 2};
+        cuuint32_t abox[2] = {(cuuint32_t)TC_BK, 1u};
+        cuuint32_t aes[2] = {1u, 1u};
+        CUresult ra = enc(&amap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(in), adims, astr, abox, aes,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (ra != CUDA_SUCCESS)
+            return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled (features) failed with code " + std::to_string((int)ra));
+    }
+
     TcParams p;
     memset(&p, 0, sizeof p);
+    p.gather4 = g4 ? 1 : 0;
     p.in = static_cast<const __nv_bfloat16*>(in);
     p.n_in = n_in;
     p.cin = (int)cin;
@@ -266,7 +291,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
         p.dynamic = use_static_schedule() ? 0 : 1;
         const int64_t ctas = p.dynamic ? p.n_tiles : std::min<int64_t>(p.n_tiles, sm_count());
         if (ctas > 0x7fffffff) return fail(SC_ERR_UNSUPPORTED, "too many row tiles for one launch");
-        conv_tc_kernel<false><<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, p);
+        conv_tc_kernel<false><<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, amap, p);
     } else {
         cudaLaunchConfig_t lc;
         memset(&lc, 0, sizeof lc);
@@ -287,7 +312,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
             max_clusters = sm_count() / 2;
         const int64_t pairs = std::min<int64_t>(p.n_tiles, max_clusters);
         lc.gridDim = dim3((unsigned)(2 * pairs));
-        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true>, wmap, p));
+        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true>, wmap, amap, p));
     }
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
