@@ -39,9 +39,11 @@
 // round-robin tiles), launched as clusters of two CTAs: a tile is 256 rows,
 // 128 per CTA; the leader issues tcgen05.mma.cta_group::2 with M = 256, each
 // CTA's A from its own shared memory and B split by N across the pair, so a
-// CTA loads and the tensor cores read only half of every weight tile.  Both halves of B
-// arrive by TMA on the leader's full barrier; the peer's "A landed" is relayed
-// by its otherwise idle MMA warp; commits are multicast to both CTAs.
+// CTA loads and the tensor cores read only half of every weight tile.  Both
+// halves of B arrive by TMA on the leader's full barrier; the peer's "A
+// landed" is relayed by its otherwise idle MMA warp (one lane per stage slot);
+// commits are multicast to both CTAs.  (Measured: a peer gathering by TMA
+// gather4 instead, with no relay, was slower.)
 // Every mbarrier wait is bounded: on expiry the device fault word is raised
 // and the CTA drains and exits instead of hanging.
 #pragma once
@@ -215,12 +217,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t* tmem_empty = bars + 3 * S + 2;
     uint64_t* sched_full = bars + 3 * S + 4;               // [TC_SCHED] response landed
     uint64_t* sched_empty = sched_full + TC_SCHED;         // [TC_SCHED] every role has read it
-    uint64_t* mask_bar = sched_empty + TC_SCHED;           // both producer warps posted their tap mask
-    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(mask_bar + 1);  // [S] PAIR relay: last step of a tile
+    uint64_t* mask_bar = sched_empty + TC_SCHED;           // every producer warp posted its tap mask
+    uint64_t* pair_bar = mask_bar + 1;                     // PAIR: the peer CTA's tap mask arrived
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(pair_bar + 1);  // [S] PAIR relay: last step of a tile
     uint32_t* tile_steps = stage_flags + S;  // [8] reduction steps per tile, ring over tiles
     // (the producers run at most S <= 8 stages, so at most 8 one-step tiles, ahead of the MMA thread)
     uint32_t* misc = tile_steps + 8;      // [0] tmem base, [1] abort
     uint32_t* mask_s = misc + 4;          // [2][TC_PW] tap masks per producer warp, by tile parity
+    uint32_t* pair_mask_s = mask_s + 2 * TC_PW;  // [2] PAIR: the peer CTA's tap mask, by tile parity
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -252,8 +256,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             // gather lanes (async, .noinc) + the producer's expect_tx arrive (+ the peer's relay);
-            // with TMA gathers one expect_tx arrive per producer warp
-            mbar_init(&full[s], (!PAIR && p.gather4) ? TC_PW : TC_PW * 32 + 1 + (PAIR ? 1 : 0));
+            // with TMA gathers only the expect_tx arrive of the stage's bytes (both CTAs' for a pair)
+            mbar_init(&full[s], p.gather4 ? 1 : TC_PW * 32 + 1 + (PAIR ? 1 : 0));
             mbar_init(&afull[s], TC_PW * 32 + 1);   // PAIR peer: gather lanes + the flags arrive
             mbar_init(&empty[s], 1);                // one tcgen05.commit
         }
@@ -266,7 +270,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&sched_empty[q], TC_PW + 1 + 4);  // producer warps, MMA thread, epilogue warps
         }
         mbar_init(mask_bar, TC_PW);
+        mbar_init(pair_bar, 1);
         misc[1] = 0;
+        misc[2] = 0xffffffffu;  // PAIR peer: stages its producers issued, once they are done
         fence_mbar_init();
         fence_proxy_async_smem();
     }
@@ -303,18 +309,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         bool ok = true;
         int64_t tile = first_tile;
         int64_t requested = 0;  // launch-control requests issued (producer warp 0)
+        int64_t issued = 0;     // stages this warp has issued
         // Contiguous map rows (no row order, or a pre-ordered map) on one CTA:
         // each producer warp reads only its own rows' map block, one tile
         // ahead, into registers (16-byte loads, all in flight at once), and
         // the two warps OR their tap masks through mask_bar.
-        const bool fast_map = !PAIR && (p.row_order == nullptr || p.nbr_ordered != nullptr);
-        const bool G4 = !PAIR && p.gather4 != 0;
+        const bool fast_map = p.row_order == nullptr || p.nbr_ordered != nullptr;
+        const bool G4 = p.gather4 != 0;
         const int32_t* map_rows = p.nbr_ordered ? p.nbr_ordered : p.nbr;
         constexpr int QV = (ROWS * TC_MAX_K / 4 + 31) / 32;  // int4 per lane for ROWS rows of <= 32 taps
         const int my_vec = ROWS * K / 4;                       // int4 of my rows' block (K * 64 / 4)
         int4 qmap[QV];
         auto load_my_map = [&](int64_t t_next) {
-            const int64_t r0 = (t_next / p.grid_y) * TILE_ROWS + pw * ROWS;
+            const int64_t r0 = (t_next / p.grid_y) * TILE_ROWS + own0;
             const int64_t left = p.n_rows - r0;
             const int n_my = left <= 0 ? 0 : (left < ROWS ? (int)left : ROWS);
             const int n_int = n_my * K;
@@ -323,7 +330,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int u = 0; u < QV; ++u) {
                 const int f4 = u * 32 + lane;
                 if (4 * f4 + 3 < n_int) {
-                    qmap[u] = __ldg(reinterpret_cast<const int4*>(blk) + f4);
+                    qmap[u] = ldg_nc_v4(reinterpret_cast<const int4*>(blk) + f4);
                 } else {
                     qmap[u].x = 4 * f4 < n_int ? __ldg(blk + 4 * f4) : -1;
                     qmap[u].y = 4 * f4 + 1 < n_int ? __ldg(blk + 4 * f4 + 1) : -1;
@@ -455,6 +462,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                         for (int w = 0; w < TC_PW; ++w) mask |= mask_s[TC_PW * (lt & 1) + w];
                     }
+                    if (PAIR && fast_map && got) {
+                        // the pair's tile spans both CTAs: swap CTA masks through the peer's smem
+                        if (pw == 0) {
+                            st_shared_cluster_u32(mapa_shared(smem_u32(pair_mask_s + (lt & 1)), rank ^ 1u), mask);
+                            mbar_arrive_cluster(mapa_shared(smem_u32(pair_bar), rank ^ 1u));
+                        }
+                        got = mbar_wait_cluster(pair_bar, (uint32_t)(lt & 1));
+                        if (got) mask |= pair_mask_s[lt & 1];
+                    }
                 }
                 if (!__shfl_sync(0xffffffffu, got, 0)) {
                     ok = false;
@@ -497,25 +513,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         break;
                     }
                     if (G4) {
-                        // A by TMA row gathers: each warp posts its bytes, then lanes 0-15 issue
+                        // A by TMA row gathers; one expect_tx (leader / single CTA) covers every byte
+                        // of the stage, the other copies only complete transactions
                         const uint32_t stage = smem_u32(a_smem + s * TC_A_BYTES);
-                        if (lane == 0) {
-                            if (pw == 0) {
-                                if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
-                                stage_flags[s] = step == n_steps - 1 ? 2u : 0u;
-                            }
-                            mbar_arrive_expect_tx(&full[s], (uint32_t)(TC_A_BYTES / TC_PW + (pw == 0 ? B_BYTES : 0)));
-                            if (pw == 0) {
-                                const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
-                                for (int q = 0; q < p.n_sub; ++q)
+                        const uint32_t bar = PAIR ? leader_full0 + (uint32_t)(s * 8) : smem_u32(&full[s]);
+                        if (lane == 0 && pw == 0) {
+                            if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
+                            if (!PAIR || leader)
+                                mbar_arrive_expect_tx(&full[s], (uint32_t)((PAIR ? 2 : 1) * (TC_A_BYTES + B_BYTES)));
+                            const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
+                            for (int q = 0; q < p.n_sub; ++q) {
+                                if (PAIR)
+                                    tma_load_3d_pair(dst + q * B_ROWS * 128, &wmap, bar, ch * TC_BK, k,
+                                                     n0 + q * p.sub_n + (int)rank * B_ROWS);
+                                else
                                     tma_load_3d(dst + q * B_ROWS * 128, &wmap, &full[s], ch * TC_BK, k,
                                                 n0 + q * p.sub_n);
                             }
                         }
-                        __syncwarp();
-                        if (lane < ROWS / 4)
-                            tma_gather4(stage + (uint32_t)((pw * ROWS + 4 * lane) * 128), &amap, &full[s], ch * TC_BK,
-                                        src[0], src[1], src[2], src[3]);
+                        if (lane < ROWS / 4) {
+                            const uint32_t dst = stage + (uint32_t)((pw * ROWS + 4 * lane) * 128);
+                            if (PAIR)
+                                tma_gather4_pair(dst, &amap, bar, ch * TC_BK, src[0], src[1], src[2], src[3]);
+                            else
+                                tma_gather4(dst, &amap, &full[s], ch * TC_BK, src[0], src[1], src[2], src[3]);
+                        }
                         if (++s == S) {
                             s = 0;
                             ph ^= 1u;
@@ -552,6 +574,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         cp_async_16(stage + r * 128 + ((j ^ (r & 7)) << 4), g, v ? 16u : 0u);
                     }
                     cp_async_arrive_noinc(&arrive_bar[s]);
+                    ++issued;
                     if (++s == S) {
                         s = 0;
                         ph ^= 1u;
@@ -561,6 +584,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (!ok) break;
             tile = nt;
         }
+        if (PAIR && pw == 0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(&misc[2]) = (uint32_t)issued;
         if (dyn && pw == 0 && lane == 0 && !ok && requested > 0) {
             // a request whose response nobody read: let it land before the CTA exits
             const int64_t q = requested - 1;
@@ -571,24 +595,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == MMA_WARP) {
         if (PAIR && !leader) {
             // ================================================ relay (pair peer)
-            // forwards "this CTA's A stage has landed" to the leader's full barrier
-            if (lane == 0) {
-                const uint32_t leader_full0 = mapa_shared(smem_u32(full), 0);
-                int s = 0;
+            // Forwards "this CTA's A stage has landed" to the leader's full
+            // barrier.  Lane l serves stage slot l, so the cluster-scope
+            // release arrives of different stages overlap; a lane stops at the
+            // first stage index at or past the producers' final count.  (With
+            // TMA gathers the peer's rows complete on the leader's barrier.)
+            if (lane < S && !p.gather4) {
+                const uint32_t lf = mapa_shared(smem_u32(full), 0) + (uint32_t)(lane * 8);
+                volatile uint32_t* total = &misc[2];
                 uint32_t ph = 0;
-                for (int64_t lt = 0; lt < my_tiles;) {
-                    if (!mbar_wait(&afull[s], ph)) {
-                        *abort_flag = 1u;
-                        break;
+                for (uint32_t it = (uint32_t)lane;; it += (uint32_t)S) {
+                    bool got = false;
+                    const uint64_t t0 = globaltimer();
+                    for (uint32_t spin = 0;; ++spin) {
+                        if (mbar_try_wait(&afull[lane], ph)) {
+                            got = true;
+                            break;
+                        }
+                        if (it >= *total) break;
+                        if ((spin & 255u) == 255u && globaltimer() - t0 > kWaitLimitNs) {
+                            raise_fault(FAULT_WAIT_TIMEOUT);
+                            *abort_flag = 1u;
+                            break;
+                        }
                     }
-                    const uint32_t flags = stage_flags[s];
+                    if (!got) break;
                     fence_proxy_async_smem();  // cp.async data -> the tensor core's reads
-                    mbar_arrive_cluster(leader_full0 + (uint32_t)(s * 8));
-                    if (++s == S) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
-                    if (flags & 2u) ++lt;
+                    mbar_arrive_cluster(lf);
+                    ph ^= 1u;
                 }
             }
         } else {
@@ -891,7 +925,7 @@ inline int tc_stg_cols(int tile_n, int cap = TC_STG_COLS) {
 inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair, int stg_cols) {
     const size_t b_bytes = (size_t)(pair ? tile_n / 2 : tile_n) * 128;
     return 1024 + (size_t)stages * (TC_A_BYTES + b_bytes) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
-           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 8 * TC_PW;
+           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 8 * TC_PW + 8 + 8;
 }
 
 }  // namespace sc

@@ -127,6 +127,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// 16-byte read-only global load kept at its place in the program (volatile),
+// so a prefetch is issued where it is written, not sunk to its first use.
+__device__ __forceinline__ int4 ldg_nc_v4(const void* p) {
+    int4 v;
+    asm volatile("ld.global.nc.v4.s32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 // One lane of the (fully active) warp, the same lane on every call.
 __device__ __forceinline__ bool elect_one() {
     uint32_t pred;
@@ -239,6 +249,31 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Store to another CTA's shared memory (a mapa address).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+// Bounded wait on a local barrier completed by another CTA's release.cluster
+// arrive, acquiring at cluster scope (the peer's stores before its arrive
+// become visible).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    for (uint32_t spin = 0;; ++spin) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((spin & 255u) == 255u && globaltimer() - t0 > kWaitLimitNs) {
+            raise_fault(FAULT_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx_addr(uint32_t cta_addr, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(cta_addr), "r"(bytes) : "memory");
 }
@@ -251,6 +286,17 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* desc,
         "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
         "l"(desc), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+// Row gather of a CTA pair: like tma_gather4, with the transaction bytes
+// counted on the pair leader's mbarrier (shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_gather4_pair(uint32_t dst, const void* desc, uint32_t bar_cluster, int x, int y0,
+                                                 int y1, int y2, int y3) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+        "l"(desc), "r"(bar_cluster), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
         : "memory");
 }
 

@@ -170,7 +170,7 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     if (plan->sub_n % 16 != 0) return false;
     plan->n_buf = tile_n <= 256 ? 2 : 1;
     plan->grid_y = (int)(cout / tile_n);
-    plan->pair = allow_pair() && plan->sub_n >= 32;
+    plan->pair = allow_pair() && plan->sub_n >= 32 && c->in_channels % 8 == 0;
     // Deepest stage ring that fits; a narrower epilogue staging buffer is
     // taken when it buys a stage (SC_TC_STG=64|128 pins the width).
     auto deepest = [&](int stg) {
@@ -223,7 +223,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     // A rows by TMA gather (tile::gather4): the features as a 2-D map [n_in, cin], 64-column boxes
     CUtensorMap amap;
     memset(&amap, 0, sizeof amap);
-    const bool g4 = !plan.pair && use_gather4() && cin % 8 == 0 && n_in > 0 && n_in < 0x7fffffff;
+    const bool g4 = use_gather4() && cin % 8 == 0 && n_in > 0 && n_in < 0x7fffffff;
     if (g4) {
         cuuint64_t adims[2] = {(cuuint64_t)cin, (cuuint64_t)n_in};
         cuuint64_t astr[1] = {(cuuint64_t)cin * 2};
