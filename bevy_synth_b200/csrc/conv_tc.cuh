@@ -86,7 +86,7 @@ struct TcParams {
     int grid_y;   // column tiles per row tile
     int64_t n_tiles;
     int dynamic;  // 1: one CTA per tile, CTAs claim unlaunched tiles by cluster launch control
-    int gather4;  // 1: A rows gathered by TMA (tile::gather4 on `amap`) instead of cp.async
+    int gather4;  // 1: A rows gathered by TMA (tile::gather4 on `amap`) instead of cp.async; 2: half of them
     int stg_cols; // epilogue staging width: a multiple of 32 dividing tile_n, <= TC_STG_COLS
     // epilogue
     const __nv_bfloat16* residual;
@@ -257,7 +257,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int s = 0; s < S; ++s) {
             // gather lanes (async, .noinc) + the producer's expect_tx arrive (+ the peer's relay);
             // with TMA gathers only the expect_tx arrive of the stage's bytes (both CTAs' for a pair)
-            mbar_init(&full[s], p.gather4 ? 1 : TC_PW * 32 + 1 + (PAIR ? 1 : 0));
+            mbar_init(&full[s], p.gather4 == 1   ? 1
+                                : p.gather4 == 2 ? (TC_PW / 2) * 32 + 1
+                                                 : TC_PW * 32 + 1 + (PAIR ? 1 : 0));
             mbar_init(&afull[s], TC_PW * 32 + 1);   // PAIR peer: gather lanes + the flags arrive
             mbar_init(&empty[s], 1);                // one tcgen05.commit
         }
@@ -315,7 +317,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ahead, into registers (16-byte loads, all in flight at once), and
         // the two warps OR their tap masks through mask_bar.
         const bool fast_map = p.row_order == nullptr || p.nbr_ordered != nullptr;
-        const bool G4 = p.gather4 != 0;
+        // gather4 == 2 (single CTA): the upper half of the producer warps gather by TMA, the lower
+        // half by cp.async, so both copy engines carry A rows
+        const bool G4 = p.gather4 == 1 || (!PAIR && p.gather4 == 2 && pw >= TC_PW / 2);
         const int32_t* map_rows = p.nbr_ordered ? p.nbr_ordered : p.nbr;
         constexpr int QV = (ROWS * TC_MAX_K / 4 + 31) / 32;  // int4 per lane for ROWS rows of <= 32 taps
         const int my_vec = ROWS * K / 4;                       // int4 of my rows' block (K * 64 / 4)
@@ -339,21 +343,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
             }
         };
+        // Launch-control requests run one tile ahead: response j names the tile after local tile
+        // j; request j + 1 goes out when tile j starts, so the response for the next tile is
+        // there when the tile starts and its map rows can be loaded a whole tile ahead.
+        int64_t consumed = 0;  // responses this warp has read
+        auto request = [&](int64_t j) -> bool {  // producer warp 0, lane 0
+            const int q = (int)(j % TC_SCHED);
+            if (!mbar_wait(&sched_empty[q], (uint32_t)(((j / TC_SCHED) & 1) ^ 1))) return false;
+            fence_proxy_async_smem();  // earlier generic reads of the slot before the async write
+            mbar_arrive_expect_tx(&sched_full[q], 16u);
+            clc_try_cancel(&sched_resp[q], &sched_full[q]);
+            requested = j + 1;
+            return true;
+        };
+        if (dyn && pw == 0 && tile >= 0) {
+            bool got = true;
+            if (lane == 0) got = request(0);
+            ok = __shfl_sync(0xffffffffu, got, 0);
+        }
         if (fast_map && tile >= 0) load_my_map(tile);
         for (int64_t lt = 0; tile >= 0 && ok; ++lt) {
             if (dyn && pw == 0) {
-                // ask for the tile after this one; its response is read when this tile's stages are issued
                 bool got = true;
-                if (lane == 0) {
-                    const int q = (int)(lt % TC_SCHED);
-                    got = mbar_wait(&sched_empty[q], (uint32_t)(((lt / TC_SCHED) & 1) ^ 1));
-                    if (got) {
-                        fence_proxy_async_smem();  // earlier generic reads of the slot before the async write
-                        mbar_arrive_expect_tx(&sched_full[q], 16u);
-                        clc_try_cancel(&sched_resp[q], &sched_full[q]);
-                        requested = lt + 1;
-                    }
-                }
+                if (lane == 0) got = request(lt + 1);
                 if (!__shfl_sync(0xffffffffu, got, 0)) {
                     ok = false;
                     break;
@@ -480,9 +492,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             if (mask == 0) mask = 1;  // a tile with no valid tap still runs one (all-zero) step
             __syncwarp();
+            // the next tile (response lt, requested a tile ago); start loading its map rows
+            int64_t nt = 0;
+            if (lane == 0) nt = next_tile(lt, true);
+            nt = __shfl_sync(0xffffffffu, nt, 0);
+            consumed = lt + 1;
+            if (nt == -2) {
+                ok = false;
+                break;
+            }
+            if (fast_map && nt >= 0) load_my_map(nt);
             const int n_steps = __popc(mask) * n_chunks;
             int step = 0;
-            int64_t nt = -1;
             for (uint32_t m = mask; m && ok; m &= m - 1) {
                 const int k = __ffs(m) - 1;
                 int32_t src[GROUPS];
@@ -496,16 +517,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 } else {
 #pragma unroll
                     for (int i = 0; i < GROUPS; ++i) src[i] = my_nbr[(i * 4 + sub) * K + k];
-                }
-                if ((m & (m - 1)) == 0) {
-                    // last tap: learn the next tile and start loading its map rows
-                    if (lane == 0) nt = next_tile(lt, true);
-                    nt = __shfl_sync(0xffffffffu, nt, 0);
-                    if (nt == -2) {
-                        ok = false;
-                        break;
-                    }
-                    if (fast_map && nt >= 0) load_my_map(nt);
                 }
                 for (int ch = 0; ch < n_chunks; ++ch, ++step) {
                     if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u))) {
@@ -550,7 +561,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         stage_flags[s] = step == n_steps - 1 ? 2u : 0u;
                         const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
                         if (!PAIR) {
-                            mbar_arrive_expect_tx(&full[s], (uint32_t)B_BYTES);
+                            mbar_arrive_expect_tx(&full[s], (uint32_t)(B_BYTES + (p.gather4 == 2 ? TC_A_BYTES / 2 : 0)));
                             for (int q = 0; q < p.n_sub; ++q)
                                 tma_load_3d(dst + q * B_ROWS * 128, &wmap, &full[s], ch * TC_BK, k,
                                             n0 + q * p.sub_n);
@@ -585,10 +596,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tile = nt;
         }
         if (PAIR && pw == 0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(&misc[2]) = (uint32_t)issued;
-        if (dyn && pw == 0 && lane == 0 && !ok && requested > 0) {
-            // a request whose response nobody read: let it land before the CTA exits
-            const int64_t q = requested - 1;
-            mbar_wait(&sched_full[q % TC_SCHED], (uint32_t)((q / TC_SCHED) & 1));
+        if (dyn && pw == 0 && lane == 0) {
+            // requests whose responses this warp did not read: let them land before the CTA exits
+            for (int64_t q = consumed; q < requested; ++q)
+                if (!mbar_wait(&sched_full[q % TC_SCHED], (uint32_t)((q / TC_SCHED) & 1))) break;
         }
         cp_async_wait<0>();
         if (!ok) *abort_flag = 1u;

@@ -115,12 +115,13 @@ static bool use_static_schedule() {
     return v;
 }
 
-static bool use_gather4() {
-    static const bool v = [] {
+// SC_TC_GATHER4: 1 = A rows by TMA gather4, 2 = half by gather4 and half by cp.async, else cp.async.
+static int gather4_mode() {
+    static const int v = [] {
         const char* e = std::getenv("SC_TC_GATHER4");
-        return e && e[0] == '1';
+        return e ? std::atoi(e) : 0;
     }();
-    return v;
+    return v == 1 || v == 2 ? v : 0;
 }
 
 static bool allow_pair() {
@@ -223,7 +224,8 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     // A rows by TMA gather (tile::gather4): the features as a 2-D map [n_in, cin], 64-column boxes
     CUtensorMap amap;
     memset(&amap, 0, sizeof amap);
-    const bool g4 = use_gather4() && cin % 8 == 0 && n_in > 0 && n_in < 0x7fffffff;
+    const int g4_mode = (cin % 8 == 0 && n_in > 0 && n_in < 0x7fffffff) ? gather4_mode() : 0;
+    const bool g4 = g4_mode == 1 || (g4_mode == 2 && !plan.pair);
     if (g4) {
         cuuint64_t adims[2] = {(cuuint64_t)cin, (cuuint64_t)n_in};
         cuuint64_t astr[1] = {(cuuint64_t)cin * 2};
@@ -238,7 +240,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
 
     TcParams p;
     memset(&p, 0, sizeof p);
-    p.gather4 = g4 ? 1 : 0;
+    p.gather4 = g4 ? g4_mode : 0;
     p.in = static_cast<const __nv_bfloat16*>(in);
     p.n_in = n_in;
     p.cin = (int)cin;
