@@ -14,6 +14,12 @@
   conv2 on the children adds the repeat-interleaved parent skip in its
   epilogue.
 * ``UpsamplePyramid``: levels of [C2S + ResBlocks].
+* ``ConvNeXtStack`` -- the production TRELLIS.2 decoder block
+  (sparse_decoder.rs:602-609; device order sparse_decoder_wgpu_ops.rs:1090-1161,
+  MLP :355-489): SubM conv whose epilogue applies bias + LayerNorm(g, b), then
+  mlp_0 (+bias, SiLU fused) and mlp_2 (+bias, + the block input fused) as
+  1x1x1 convs over the identity map -- three tcgen05 launches per block, no
+  separate LayerNorm / SiLU / add passes.
 """
 from __future__ import annotations
 
@@ -26,6 +32,7 @@ from . import flex_gmm as F
 
 RESBLOCK_LN_EPS = 1e-5  # sparse_structure_decoder.rs:22
 C2S_LN_EPS = 1e-6       # sparse_decoder.rs:43 (LAYER_NORM32_EPS)
+CONVNEXT_LN_EPS = 1e-6  # the same constant (sparse_decoder_wgpu_ops.rs:1137-1144)
 
 
 def _dev(a, device, dtype=None):
@@ -195,3 +202,71 @@ class SubmStack:
     def flops(self, nbr: torch.Tensor) -> float:
         p = float((nbr >= 0).sum())
         return sum(2.0 * p * c.in_channels * c.out_channels for c in self.cfgs)
+
+
+@dataclass
+class ConvNeXtParams:
+    w: torch.Tensor       # [C, 3, 3, 3, C]
+    b: torch.Tensor
+    norm_g: torch.Tensor
+    norm_b: torch.Tensor
+    w0: torch.Tensor      # [hidden, C]
+    b0: torch.Tensor
+    w2: torch.Tensor      # [C, hidden]
+    b2: torch.Tensor
+
+    @staticmethod
+    def from_numpy(p: dict, device, dtype=torch.bfloat16) -> "ConvNeXtParams":
+        f32 = torch.float32
+        return ConvNeXtParams(_dev(p["w"], device, dtype), _dev(p["b"], device, f32), _dev(p["norm_g"], device, f32),
+                              _dev(p["norm_b"], device, f32), _dev(p["w0"], device, dtype),
+                              _dev(p["b0"], device, f32), _dev(p["w2"], device, dtype), _dev(p["b2"], device, f32))
+
+
+class ConvNeXtStack:
+    """ConvNeXt decoder blocks of one stage (convnext_blocks_forward_wgpu_tensor,
+    sparse_decoder_wgpu_ops.rs:1090-1161): the neighbor map is built once per
+    stage and shared by the blocks."""
+
+    def __init__(self, blocks: list[ConvNeXtParams]):
+        self.blocks = blocks
+        c = blocks[0].w.shape[0]
+        self.channels = c
+        self.hidden = blocks[0].w0.shape[0]
+        self.cfg = F.SparseSubmConvConfig.subm3(c, c)
+
+    def launches(self) -> int:
+        return 3 * len(self.blocks)
+
+    def forward(self, x: torch.Tensor, nbr: torch.Tensor, schedule=None, bufs: dict | None = None) -> torch.Tensor:
+        n, c = x.shape
+        if c != self.channels:
+            raise F.SparseConvError(F._lib.SC_ERR_INVALID, f"decoder wgpu convnext tensor dims mismatch: got=[{n},{c}] "
+                                        f"expected=[{n},{self.channels}]")
+        bufs = {} if bufs is None else bufs
+
+        def buf(name, cols):
+            t = bufs.get(name)
+            if t is None or t.shape != (n, cols) or t.dtype != x.dtype:
+                t = torch.empty((n, cols), dtype=x.dtype, device=x.device)
+                bufs[name] = t
+            return t
+
+        cur = x
+        for i, p in enumerate(self.blocks):
+            h = F.sparse_subm_conv_forward(
+                self.cfg, cur, nbr, p.w, p.b,
+                F.Epilogue(layer_norm=True, ln_eps=CONVNEXT_LN_EPS, ln_gamma=p.norm_g, ln_beta=p.norm_b,
+                           schedule=schedule),
+                out=buf("h", c))
+            hid = F.linear_forward(h, p.w0, p.b0, F.Epilogue(silu=True), out=buf("hid", self.hidden))
+            nxt = buf(f"x{i % 2}", c)
+            cur = F.linear_forward(hid, p.w2, p.b2, F.Epilogue(residual=cur), out=nxt)
+        return cur
+
+    def flops(self, nbr: torch.Tensor) -> float:
+        """Algorithmic FLOPs: 2*P*C^2 for the conv, 2*N*C*hidden per linear."""
+        P = float((nbr >= 0).sum())
+        n = nbr.shape[0]
+        per = 2.0 * P * self.channels ** 2 + 2 * 2.0 * n * self.channels * self.hidden
+        return per * len(self.blocks)

@@ -288,6 +288,46 @@ def sparse_subm_conv_forward_cubecl(config: SparseSubmConvConfig, input: torch.T
     return sparse_subm_conv_forward(config, input, neighbor_rows, weight, bias)
 
 
+_IDENTITY_ROWS: dict = {}
+
+
+def identity_rows(n: int, device) -> torch.Tensor:
+    """[n, 1] int32 map with row r -> r: a dense per-row layer as a 1x1x1
+    sparse conv.  Cached per device (grown on demand, sliced)."""
+    key = torch.device(device)
+    t = _IDENTITY_ROWS.get(key)
+    if t is None or t.shape[0] < n:
+        t = torch.arange(max(n, 1024), dtype=torch.int32, device=key).view(-1, 1)
+        _IDENTITY_ROWS[key] = t
+    return t[:n]
+
+
+def linear_forward(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                   epilogue: Epilogue | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Linear layer ``out = input @ weight.T + bias`` with the conv's fused
+    epilogue (SiLU, residual, LayerNorm), run as a 1x1x1 sparse conv over the
+    identity map, so it takes the same tcgen05 gather-GEMM as the convs.
+    ``weight`` is [out, in] row-major as PyTorch stores linear layers (the
+    reference's LinearLayer, burn_trellis src/runtime_model/sparse_decoder.rs:623-631;
+    math of ``linear_forward``, sparse_decoder_wgpu_ops.rs:1-60: bias first,
+    then the GEMM accumulates)."""
+    _require_cuda("input", input)
+    if input.dim() != 2 or weight.dim() != 2:
+        raise SparseConvError(_lib.SC_ERR_INVALID, "linear input and weight must be 2-D")
+    rows, cin = input.shape
+    cout = weight.shape[0]
+    if weight.shape[1] != cin:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"linear: invalid input len {rows * cin}, expected {rows * weight.shape[1]} "
+                              f"(rows={rows} in_channels={weight.shape[1]})")
+    if bias is not None and bias.shape[0] != cout:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"linear: bias len {bias.shape[0]} does not match out_channels {cout}")
+    cfg = SparseSubmConvConfig(cin, cout, 1, 1, 1)
+    return sparse_subm_conv_forward(cfg, input, identity_rows(rows, input.device),
+                                    weight.reshape(cout, 1, 1, 1, cin), bias, epilogue, out=out)
+
+
 def uses_tensor_cores(config: SparseSubmConvConfig, dtype: torch.dtype) -> bool:
     f = ctypes.c_int32(0)
     c = config.c()

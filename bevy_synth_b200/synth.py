@@ -149,6 +149,20 @@ def c2s_params(rng, cin: int, cout: int) -> dict:
     }
 
 
+def convnext_params(rng, c: int, hidden: int) -> dict:
+    """A ConvNeXt decoder block: SubM C->C, LayerNorm(g, b), Linear C->hidden,
+    Linear hidden->C (PyTorch [out, in] layout), weights N(0, 0.02^2)."""
+    return {
+        "w": normal_weight(rng, c, c), "b": (0.02 * rng.standard_normal(c)).astype(np.float32),
+        "norm_g": (1.0 + 0.1 * rng.standard_normal(c)).astype(np.float32),
+        "norm_b": (0.1 * rng.standard_normal(c)).astype(np.float32),
+        "w0": (0.02 * rng.standard_normal((hidden, c))).astype(np.float32),
+        "b0": (0.02 * rng.standard_normal(hidden)).astype(np.float32),
+        "w2": (0.02 * rng.standard_normal((c, hidden))).astype(np.float32),
+        "b2": (0.02 * rng.standard_normal(c)).astype(np.float32),
+    }
+
+
 # --------------------------------------------------------------------------
 # The five configurations
 # --------------------------------------------------------------------------
@@ -248,3 +262,13 @@ def config5(seed: int = 0, grid: int = 1024, shells: int = 32) -> Workload:
     ws = [normal_weight(rng, co, ci) for ci, co in chans]
     bs = [np.zeros(co, np.float32) for _, co in chans]
     return Workload("cfg5_sharded_grid_bf16", coords, feats, {"w": ws, "b": bs, "chans": chans}, {})
+
+
+def convnext_stage(seed: int = 0, channels: int = 256, hidden: int = 1024, blocks: int = 2) -> Workload:
+    """A ConvNeXt decoder stage (not a BASELINE configuration; the production
+    TRELLIS.2 decoder block): config 2's 128^3 union of shells, C=256 with a
+    4x MLP, bf16."""
+    w2 = config2(seed, blocks=1, channels=channels)
+    rng = np.random.default_rng(seed + 7)
+    params = [convnext_params(rng, channels, hidden) for _ in range(blocks)]
+    return Workload("convnext_stage_bf16_256", w2.coords, w2.feats, params, {})

@@ -11,6 +11,10 @@ primitives in ``oracle/__init__.py``:
   ``LN(no affine)->SiLU->SubM(Cout->Cout)`` on children plus the skip
   (parent row as [8, Cin/8], row c, each channel repeated Cout/(Cin/8) times),
   LayerNorm eps 1e-6 (sparse_decoder.rs:43).
+* ConvNeXt decoder block (sparse_decoder.rs:602-609; device order
+  sparse_decoder_wgpu_ops.rs:1090-1161 with the MLP at :355-489; host order
+  sparse_decoder_runtime_impl.rs:689-755): ``h = LN(g,b)(SubM(x))``,
+  ``h = SiLU(mlp_0(h))``, ``out = mlp_2(h) + x``; LayerNorm eps 1e-6.
 
 Precision.  ``bf16=True`` mirrors where the CUDA path stores bf16: inputs and
 weights are rounded to bf16 (RNE, burn_flex_gmm/src/wgpu.rs:57-67); every
@@ -27,6 +31,7 @@ from . import (DUP_LOWEST, OracleConfig, bf16_round, build_neighbor_rows, channe
 
 RESBLOCK_LN_EPS = 1e-5  # sparse_structure_decoder.rs:22
 C2S_LN_EPS = 1e-6       # sparse_decoder.rs:43 (LAYER_NORM32_EPS)
+CONVNEXT_LN_EPS = 1e-6  # the same LAYER_NORM32_EPS (sparse_decoder_wgpu_ops.rs:1137-1144)
 
 
 def _q(x, bf16: bool):
@@ -37,6 +42,37 @@ def conv(x, nbr, w, b, bf16: bool, threads: int = 8):
     cout, kd, kh, kw, cin = w.shape
     cfg = OracleConfig(cin, cout, kd, kh, kw)
     return subm_conv_flex(cfg, _q(w, bf16), b, _q(x, bf16), nbr, threads=threads)
+
+
+def linear(x, w, b, bf16: bool, threads: int = 8):
+    """Linear layer, weight [out, in] (burn_trellis sparse_decoder.rs:623-631):
+    ``linear_forward`` (sparse_decoder_wgpu_ops.rs:1-60) writes the bias into
+    every output row, then accumulates input @ weight.T with sgemm (beta=1) --
+    the flex conv's order, so it is the flex conv with one tap over the
+    identity rows."""
+    w = np.asarray(w, np.float32)
+    cout, cin = w.shape
+    cfg = OracleConfig(cin, cout, 1, 1, 1)
+    n = np.asarray(x).shape[0]
+    ident = np.arange(n, dtype=np.int32).reshape(n, 1)
+    return subm_conv_flex(cfg, _q(w, bf16).reshape(cout, 1, 1, 1, cin), b, _q(x, bf16), ident, threads=threads)
+
+
+def convnext_block(x, nbr, p, bf16: bool, threads: int = 8):
+    """One ConvNeXt decoder block; returns the fp32 (unrounded) output."""
+    x = _q(x, bf16)
+    h = _q(layer_norm(conv(x, nbr, p["w"], p["b"], bf16, threads), p["norm_g"], p["norm_b"], CONVNEXT_LN_EPS),
+           bf16)
+    h = _q(silu(linear(h, p["w0"], p["b0"], bf16, threads)), bf16)
+    return linear(h, p["w2"], p["b2"], bf16, threads) + x
+
+
+def convnext_stack(x, nbr, blocks, bf16: bool, threads: int = 8):
+    """Blocks in order, each output rounded where the CUDA path stores it."""
+    y = np.asarray(x, np.float32)
+    for p in blocks:
+        y = _q(convnext_block(y, nbr, p, bf16, threads), bf16)
+    return y
 
 
 def neighbor_map(coords, kernel=(3, 3, 3)):

@@ -104,3 +104,46 @@ def test_resblock_stack_with_schedule_matches_plain(cuda_device):
     b = stack.forward(xt, nbr, schedule=F.neighbor_schedule(cfg, nbr)).float()
     assert rel_l2(b.cpu().numpy(), a.cpu().numpy()) <= 1e-6
     assert_no_fault()
+
+
+@pytest.mark.parametrize("rows,cin,cout,dtype,tol", [(5000, 256, 1024, torch.bfloat16, 1e-2),
+                                                     (3000, 1024, 256, torch.bfloat16, 1e-2),
+                                                     (777, 96, 64, torch.bfloat16, 1e-2),
+                                                     (1000, 64, 64, torch.float32, 1e-4)])
+def test_linear_forward(cuda_device, rows, cin, cout, dtype, tol):
+    """Linear layer (sparse_decoder_wgpu_ops.rs:1-60) as a 1x1x1 conv over the identity map."""
+    rng = np.random.default_rng(rows)
+    x = rng.standard_normal((rows, cin)).astype(np.float32)
+    w = (0.05 * rng.standard_normal((cout, cin))).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    got = F.linear_forward(to_dev(x, dtype), to_dev(w, dtype), to_dev(b)).float().cpu().numpy()
+    ref = OB.linear(x, w, b, bf16=dtype == torch.bfloat16)
+    if dtype == torch.bfloat16:
+        ref = oracle.bf16_round(ref)
+    assert rel_l2(got, ref) <= tol, rel_l2(got, ref)
+    assert_no_fault()
+
+
+def test_linear_forward_errors(cuda_device):
+    x = to_dev(np.zeros((4, 64), np.float32), torch.bfloat16)
+    with pytest.raises(F.SparseConvError, match="invalid input len"):
+        F.linear_forward(x, to_dev(np.zeros((32, 48), np.float32), torch.bfloat16))
+    with pytest.raises(F.SparseConvError, match="bias len 16 does not match out_channels 32"):
+        F.linear_forward(x, to_dev(np.zeros((32, 64), np.float32), torch.bfloat16), to_dev(np.zeros(16, np.float32)))
+
+
+@pytest.mark.parametrize("c,hidden,nblocks", [(64, 256, 2), (256, 1024, 2)])
+def test_convnext_stack(cuda_device, c, hidden, nblocks):
+    """ConvNeXt decoder blocks (sparse_decoder_wgpu_ops.rs:1090-1161, MLP :355-489) vs the oracle."""
+    coords = shell()
+    rng = np.random.default_rng(c + hidden)
+    x = rng.standard_normal((coords.shape[0], c)).astype(np.float32)
+    params = [synth.convnext_params(rng, c, hidden) for _ in range(nblocks)]
+    cfg = F.SparseSubmConvConfig.subm3(c, c)
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords))
+    stack = blocks.ConvNeXtStack([blocks.ConvNeXtParams.from_numpy(p, dev()) for p in params])
+    for sched in (None, F.neighbor_schedule(cfg, nbr)):
+        got = stack.forward(to_dev(x, torch.bfloat16), nbr, sched).float().cpu().numpy()
+        ref = OB.convnext_stack(x, nbr.cpu().numpy(), params, bf16=True)
+        assert rel_l2(got, ref) <= 1e-2, rel_l2(got, ref)
+    assert_no_fault()
