@@ -145,30 +145,37 @@ struct Staging {
     __device__ __forceinline__ uint8_t* at(int r, int u) const { return base + (r * (units + 1) + u) * 16; }
 };
 
-// Staged rows -> global rows orow (per lane = row; < 0 skipped), columns
-// [col0, col0 + 8*units) of a row-major matrix with leading dimension ld.
+// Lane's staged row -> global row orow (< 0: skipped), columns [col0,
+// col0 + 8*units) of a row-major matrix with leading dimension ld, as one
+// bulk copy (TMA engine, no load/store-unit traffic).  The staged row was
+// written by this lane; callers wait for the copy's reads (stg_reuse) before
+// writing the staging buffer again.
 __device__ __forceinline__ void store_staged_rows(const Staging& st, int64_t orow, __nv_bfloat16* dst,
                                                   int64_t ld, int col0, int lane) {
-    const int total = 32 * st.units;
-    for (int idx = lane; idx < total; idx += 32) {
-        const int r = idx / st.units, u = idx - r * st.units;
-        const int64_t o = __shfl_sync(0xffffffffu, orow, r);
-        if (o >= 0)
-            *reinterpret_cast<uint4*>(dst + o * ld + col0 + u * 8) = *reinterpret_cast<const uint4*>(st.at(r, u));
-    }
+    fence_proxy_async_smem();  // this lane's staging writes -> the bulk copy's reads
+    if (orow >= 0) bulk_store(dst + orow * ld + col0, smem_u32(st.at(lane, 0)), (uint32_t)(st.units * 16));
+    bulk_commit();
 }
 
-// Global rows rrow (per lane = row; < 0 gives zeros) -> staged rows.
-__device__ __forceinline__ void load_staged_rows(const Staging& st, int64_t rrow, const __nv_bfloat16* src,
-                                                 int64_t ld, int col0, int lane) {
-    const int total = 32 * st.units;
-    for (int idx = lane; idx < total; idx += 32) {
-        const int r = idx / st.units, u = idx - r * st.units;
-        const int64_t o = __shfl_sync(0xffffffffu, rrow, r);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (o >= 0) v = __ldg(reinterpret_cast<const uint4*>(src + o * ld + col0 + u * 8));
-        *reinterpret_cast<uint4*>(st.at(r, u)) = v;
+// The staging buffer may be written again: this lane's bulk stores have read it.
+__device__ __forceinline__ void stg_reuse() { bulk_wait_read_all(); }
+
+// Global row rrow (per lane = row; < 0 gives zeros) -> the lane's staged row,
+// by bulk copy completing on the warp's barrier `bar` (phase `ph`, flipped).
+__device__ __forceinline__ bool load_staged_rows(const Staging& st, int64_t rrow, const __nv_bfloat16* src,
+                                                 int64_t ld, int col0, int lane, uint64_t* bar, uint32_t& ph) {
+    const uint32_t bytes = (uint32_t)(st.units * 16);
+    const uint32_t n_rows = (uint32_t)__popc(__ballot_sync(0xffffffffu, rrow >= 0));
+    if (lane == 0) mbar_arrive_expect_tx(bar, n_rows * bytes);
+    __syncwarp();
+    if (rrow >= 0) {
+        bulk_load(smem_u32(st.at(lane, 0)), src + rrow * ld + col0, bytes, bar);
+    } else {
+        for (int u = 0; u < st.units; ++u) *reinterpret_cast<uint4*>(st.at(lane, u)) = make_uint4(0, 0, 0, 0);
     }
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, ph));
+    ph ^= 1u;
+    return ok;
 }
 
 __device__ __forceinline__ void add_param32(float (&v)[32], const float* p, bool mul) {
@@ -219,7 +226,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t* sched_empty = sched_full + TC_SCHED;         // [TC_SCHED] every role has read it
     uint64_t* mask_bar = sched_empty + TC_SCHED;           // every producer warp posted its tap mask
     uint64_t* pair_bar = mask_bar + 1;                     // PAIR: the peer CTA's tap mask arrived
-    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(pair_bar + 1);  // [S] PAIR relay: last step of a tile
+    uint64_t* res_bar = pair_bar + 1;                      // [4] per epilogue warp: staged residual rows landed
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(res_bar + 4);  // [S] PAIR relay: last step of a tile
     uint32_t* tile_steps = stage_flags + S;  // [8] reduction steps per tile, ring over tiles
     // (the producers run at most S <= 8 stages, so at most 8 one-step tiles, ahead of the MMA thread)
     uint32_t* misc = tile_steps + 8;      // [0] tmem base, [1] abort
@@ -273,6 +281,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         mbar_init(mask_bar, TC_PW);
         mbar_init(pair_bar, 1);
+        for (int w = 0; w < 4; ++w) mbar_init(&res_bar[w], 1);  // lane 0's expect_tx arrive
         misc[1] = 0;
         misc[2] = 0xffffffffu;  // PAIR peer: stages its producers issued, once they are done
         fence_mbar_init();
@@ -720,6 +729,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         Staging st;
         st.units = stg_units;
         st.base = stg_smem + warp * 32 * (stg_units + 1) * 16;
+        uint32_t res_ph = 0;  // phase of this warp's residual barrier
         const int t = tid;  // TMEM lane == tile row (of this CTA's half)
         const int W = p.ln_width;
         const bool multi = p.ln != 0 || p.out2 != nullptr;
@@ -776,10 +786,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
             if (!multi) {
                 for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
-                    if (dense_res) {
-                        load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane);
-                        __syncwarp();
-                    }
+                    stg_reuse();
+                    if (dense_res && !load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane, &res_bar[warp], res_ph))
+                        *abort_flag = 1u;
                     for (int c = g0; c < g0 + stg_cols; c += 32) {
                         float v[32];
                         compute_y(c, g0, v);
@@ -797,10 +806,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 // pass 1: y -> TMEM (residual folded in) and per-group sums
                 float sum[4] = {0.f, 0.f, 0.f, 0.f};  // <= 4 LayerNorm groups per tile
                 for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
-                    if (dense_res) {
-                        load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane);
-                        __syncwarp();
-                    }
+                    stg_reuse();
+                    if (dense_res && !load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane, &res_bar[warp], res_ph))
+                        *abort_flag = 1u;
                     for (int c = g0; c < g0 + stg_cols; c += 32) {
                         float v[32];
                         compute_y(c, g0, v);
@@ -856,6 +864,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 // pass 3: out = y when a second output is requested
                 if (p.out2) {
                     for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
+                        stg_reuse();
                         for (int c = g0; c < g0 + stg_cols; c += 32) {
                             float v[32];
                             tmem_ld32(lane_addr + c, v);
@@ -869,6 +878,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 // pass 4: post(y) = [LayerNorm(gamma, beta)] -> [SiLU]
                 __nv_bfloat16* dst = p.out2 ? p.out2 : p.out;
                 for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
+                    stg_reuse();
                     for (int c = g0; c < g0 + stg_cols; c += 32) {
                         float v[32];
                         tmem_ld32(lane_addr + c, v);
@@ -909,6 +919,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 break;
             }
         }
+        bulk_wait_all();  // every output row written before the CTA leaves
     }
 
     tc_fence_before();
@@ -936,7 +947,7 @@ inline int tc_stg_cols(int tile_n, int cap = TC_STG_COLS) {
 inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair, int stg_cols) {
     const size_t b_bytes = (size_t)(pair ? tile_n / 2 : tile_n) * 128;
     return 1024 + (size_t)stages * (TC_A_BYTES + b_bytes) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
-           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 8 * TC_PW + 8 + 8;
+           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 8 * TC_PW + 8 + 8 + 4 * 8;
 }
 
 }  // namespace sc
