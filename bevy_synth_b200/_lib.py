@@ -29,7 +29,8 @@ EXPORTED = (
     "sc_neighbor_workspace_bytes", "sc_neighbor_map", "sc_neighbor_map_query", "sc_neighbor_status",
     "sc_neighbor_map_noalloc", "sc_neighbor_schedule_scratch_bytes", "sc_neighbor_schedule",
     "sc_subm_conv_forward", "sc_conv_uses_tensor_cores", "sc_layer_norm_act", "sc_bf16_round",
-    "sc_cast", "sc_subdivide_scratch_bytes", "sc_subdivide", "sc_gather_rows",
+    "sc_cast", "sc_subdivide_scratch_bytes", "sc_subdivide", "sc_gather_rows", "sc_subdiv_head",
+    "sc_patchify3d_scratch_bytes", "sc_patchify3d_forward",
 )
 
 
@@ -49,6 +50,11 @@ class ScConvConfig(ctypes.Structure):
         ("groups", ctypes.c_int64),
         ("axis_order", ctypes.c_int32 * 3), ("axis_sign", ctypes.c_int32 * 3),
     ]
+
+
+class ScPatchify3dConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int64) for n in ("in_channels", "out_channels", "frames", "height", "width",
+                                              "tubelet_size", "patch_h", "patch_w")]
 
 
 class ScEpilogue(ctypes.Structure):
@@ -94,6 +100,11 @@ _SIGS = {
     "sc_bf16_round": ([_P, _I64, _P, _P], ctypes.c_int),
     "sc_cast": ([ctypes.c_int, ctypes.c_int, _P, _I64, _P, _P], ctypes.c_int),
     "sc_gather_rows": ([_P, _I64, _I64, _P, _I64, _P, _P], ctypes.c_int),
+    "sc_subdiv_head": ([ctypes.c_int, _P, _I64, _I64, _P, _P, ctypes.c_float, _P, ctypes.c_int, _P, _P, _P],
+                       ctypes.c_int),
+    "sc_patchify3d_scratch_bytes": ([_P, _I64, ctypes.c_int, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "sc_patchify3d_forward": ([_P, ctypes.c_int, _P, _I64, _P, _I64, _P, _P, _P, ctypes.c_size_t, _P, _P],
+                              ctypes.c_int),
     "sc_subdivide_scratch_bytes": ([_I64, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "sc_subdivide": ([_P, _P, _I64, _I64, _P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _P], ctypes.c_int),
 }

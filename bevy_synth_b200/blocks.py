@@ -115,12 +115,15 @@ class C2SParams:
     b1: torch.Tensor
     w2: torch.Tensor   # [Cout, 3, 3, 3, Cout]
     b2: torch.Tensor
+    w_sub: torch.Tensor | None = None  # to_subdiv [8, Cin] (used when no mask is given)
+    b_sub: torch.Tensor | None = None
 
     @staticmethod
     def from_numpy(p: dict, device, dtype=torch.bfloat16) -> "C2SParams":
         f32 = torch.float32
+        sub = (_dev(p["w_sub"], device, dtype), _dev(p["b_sub"], device, f32)) if "w_sub" in p else (None, None)
         return C2SParams(_dev(p["ln1_g"], device, f32), _dev(p["ln1_b"], device, f32), _dev(p["w1"], device, dtype),
-                         _dev(p["b1"], device, f32), _dev(p["w2"], device, dtype), _dev(p["b2"], device, f32))
+                         _dev(p["b1"], device, f32), _dev(p["w2"], device, dtype), _dev(p["b2"], device, f32), *sub)
 
 
 class C2SUpsampleBlock:
@@ -131,9 +134,16 @@ class C2SUpsampleBlock:
         self.cfg1 = F.SparseSubmConvConfig.subm3(self.cin, 8 * self.cout)
         self.cfg2 = F.SparseSubmConvConfig.subm3(self.cout, self.cout)
 
-    def forward(self, coords: torch.Tensor, x: torch.Tensor, mask: torch.Tensor, nbr_parent=None):
-        """Returns (child_coords, child_feats, child_nbr)."""
+    def forward(self, coords: torch.Tensor, x: torch.Tensor, mask: torch.Tensor | None = None, nbr_parent=None,
+                threshold: float = 0.0):
+        """Returns (child_coords, child_feats, child_nbr).  Without ``mask`` the
+        children come from the to_subdiv head on x (logits > threshold)."""
         p = self.p
+        if mask is None:
+            if p.w_sub is None:
+                raise F.SparseConvError(F._lib.SC_ERR_INVALID,
+                                        "decoder stage requires guide_subdivisions but none were provided")
+            _, mask = F.subdivision_head(x, p.w_sub, p.b_sub, threshold, return_logits=False)
         h = F.layer_norm_affine_silu_forward(x, p.ln1_g, p.ln1_b, C2S_LN_EPS)
         child_row, child_coords, skip_off = F.subdivide(coords, mask, self.cin)
         n_child = child_coords.shape[0]

@@ -110,4 +110,86 @@ __global__ void permute_rows_kernel(const int32_t* __restrict__ nbr, const int32
     ordered[i] = __ldg(nbr + (int64_t)__ldg(order + p) * K + k);
 }
 
+// Subdivision head: logits[r, c] = bias[c] + sum_k x[r, k] * W[c, k] for the
+// 8 children (the decoder's to_subdiv linear layer, fp32 accumulate),
+// optionally centred on the row's mean, and mask[r, c] = logit > thr[c].
+// One warp per row; each lane accumulates a strided slice of the channels.
+struct SubdivThresholds {
+    float t[8];
+};
+template <typename T>
+__global__ void subdiv_head_kernel(const T* __restrict__ x, int64_t n, int c, const T* __restrict__ w,
+                                   const float* __restrict__ bias, SubdivThresholds thr, int center,
+                                   float* __restrict__ logits, uint8_t* __restrict__ mask) {
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n) return;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const T* xr = x + r * c;
+    for (int k = lane; k < c; k += 32) {
+        const float v = to_f32(xr[k]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += v * to_f32(__ldg(w + (int64_t)j * c + k));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    float lg[8];
+    float mean = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        lg[j] = acc[j] + (bias ? __ldg(bias + j) : 0.f);
+        mean += lg[j];
+    }
+    mean *= 0.125f;
+    if (lane < 8) {
+        float v = lg[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j)
+            if (lane == j) v = lg[j];
+        if (center) v -= mean;
+        if (logits) logits[r * 8 + lane] = v;
+        mask[r * 8 + lane] = v > thr.t[lane] ? 1 : 0;
+    }
+}
+
+// Sparse 3-D patchify, gather half: for each coordinate row (batch,
+// tubelet, patch_row, patch_col) the patch of the dense input [B, Cin, T, H, W]
+// flattened in (c, dt, py, px) order -> im2col[row, K].  Coordinates outside
+// the grid raise the fault word and give a zero row.
+struct PatchGeom {
+    int64_t cin, frames, height, width, batches;
+    int tub, ph, pw;
+};
+template <typename T>
+__global__ void patch_gather_kernel(const T* __restrict__ input, const int4* __restrict__ coords, int64_t rows,
+                                    PatchGeom g, T* __restrict__ out) {
+    const int64_t K = g.cin * g.tub * g.ph * g.pw;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * K) return;
+    const int64_t r = i / K;
+    const int64_t k0 = i - r * K;
+    int64_t kk = k0;
+    const int px = (int)(kk % g.pw);
+    kk /= g.pw;
+    const int py = (int)(kk % g.ph);
+    kk /= g.ph;
+    const int dt = (int)(kk % g.tub);
+    const int64_t c = kk / g.tub;
+    const int4 q = __ldg(coords + r);
+    const int64_t t = (int64_t)q.y * g.tub + dt, y = (int64_t)q.z * g.ph + py, x = (int64_t)q.w * g.pw + px;
+    if (q.x < 0 || q.x >= g.batches || q.y < 0 || t >= g.frames || q.z < 0 || y >= g.height || q.w < 0 ||
+        x >= g.width) {
+        if (k0 == 0) raise_fault(FAULT_BAD_NEIGHBOR);
+        out[i] = T(0.f);
+        return;
+    }
+    out[i] = __ldg(input + ((((int64_t)q.x * g.cin + c) * g.frames + t) * g.height + y) * g.width + x);
+}
+
+__global__ void iota_kernel(int32_t* __restrict__ out, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = (int32_t)i;
+}
+
 }  // namespace sc

@@ -6,6 +6,7 @@
 // 369-473 validate_tensor_shapes) and reports them as SC_ERR_INVALID with a
 // message, as the reference returns Err(String).
 #include <cub/device/device_radix_sort.cuh>
+#include <cmath>
 #include <cub/device/device_scan.cuh>
 
 #include <algorithm>
@@ -693,6 +694,122 @@ int sc_subdivide_scratch_bytes(int64_t n_parent, size_t* bytes) {
     if (n_parent < 0 || !bytes) return fail(SC_ERR_INVALID, "invalid subdivide scratch query");
     const size_t a = ((size_t)(n_parent + 1) * 4 + 255) / 256 * 256;
     *bytes = 2 * a + subdiv_cub_bytes(n_parent) + 256;
+    return SC_OK;
+}
+
+static int validate_patchify(const sc_patchify3d_config* c) {
+    if (!c) return fail(SC_ERR_INVALID, "null config");
+    if (c->in_channels <= 0 || c->out_channels <= 0)
+        return fail(SC_ERR_INVALID, "sparse patchify channel dimensions must be non-zero");
+    if (c->frames <= 0 || c->height <= 0 || c->width <= 0)
+        return fail(SC_ERR_INVALID, "sparse patchify input dimensions must be non-zero");
+    if (c->tubelet_size <= 0 || c->patch_h <= 0 || c->patch_w <= 0)
+        return fail(SC_ERR_INVALID, "sparse patchify patch dimensions must be non-zero");
+    if (c->frames % c->tubelet_size != 0)
+        return fail(SC_ERR_INVALID, "sparse patchify frames must be divisible by tubelet_size: " +
+                                        std::to_string(c->frames) + " % " + std::to_string(c->tubelet_size) + " != 0");
+    if (c->height % c->patch_h != 0)
+        return fail(SC_ERR_INVALID, "sparse patchify height must be divisible by patch_h: " +
+                                        std::to_string(c->height) + " % " + std::to_string(c->patch_h) + " != 0");
+    if (c->width % c->patch_w != 0)
+        return fail(SC_ERR_INVALID, "sparse patchify width must be divisible by patch_w: " +
+                                        std::to_string(c->width) + " % " + std::to_string(c->patch_w) + " != 0");
+    return SC_OK;
+}
+
+int sc_patchify3d_scratch_bytes(const sc_patchify3d_config* c, int64_t rows, sc_dtype dtype, size_t* bytes) {
+    if (int rc = validate_patchify(c)) return rc;
+    if (!bytes || rows < 0) return fail(SC_ERR_INVALID, "invalid arguments");
+    const int64_t K = c->in_channels * c->tubelet_size * c->patch_h * c->patch_w;
+    const size_t es = dtype == SC_DTYPE_BF16 ? 2 : 4;
+    *bytes = align256((size_t)rows * 4) + align256((size_t)rows * (size_t)K * es);
+    return SC_OK;
+}
+
+int sc_patchify3d_forward(const sc_patchify3d_config* c, sc_dtype dtype, const void* input, int64_t input_elems,
+                          const int32_t* coords, int64_t rows, const void* weight, const float* bias, void* scratch,
+                          size_t scratch_bytes, void* out, void* stream) {
+    if (int rc = validate_patchify(c)) return rc;
+    if (dtype != SC_DTYPE_F32 && dtype != SC_DTYPE_BF16) return fail(SC_ERR_INVALID, "sparse patchify: bad dtype");
+    const int64_t per_batch = c->in_channels * c->frames * c->height * c->width;
+    if (input_elems < 0 || input_elems % per_batch != 0)
+        return fail(SC_ERR_INVALID, "sparse patchify input len mismatch: got " + std::to_string(input_elems) +
+                                        " expected a multiple of " + std::to_string(per_batch));
+    if (rows < 0) return fail(SC_ERR_INVALID, "invalid row count");
+    if (rows == 0) return SC_OK;
+    if (rows > 0x7fffffff) return fail(SC_ERR_UNSUPPORTED, "sparse patchify: too many rows");
+    size_t need = 0;
+    sc_patchify3d_scratch_bytes(c, rows, dtype, &need);
+    if (!scratch || scratch_bytes < need)
+        return fail(SC_ERR_CAPACITY, "sparse patchify scratch too small: need " + std::to_string(need) + " bytes");
+    if (!input || !coords || !weight || !out) return fail(SC_ERR_INVALID, "null pointer");
+    if (!aligned16(coords)) return fail(SC_ERR_INVALID, "coordinates must be 16-byte aligned");
+    const int64_t K = c->in_channels * c->tubelet_size * c->patch_h * c->patch_w;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int32_t* ident = static_cast<int32_t*>(scratch);
+    void* cols = static_cast<uint8_t*>(scratch) + align256((size_t)rows * 4);
+    iota_kernel<<<grid1d(rows, 256), 256, 0, st>>>(ident, rows);
+    SC_CUDA_TRY(cudaGetLastError());
+    PatchGeom g;
+    g.cin = c->in_channels;
+    g.frames = c->frames;
+    g.height = c->height;
+    g.width = c->width;
+    g.batches = input_elems / per_batch;
+    g.tub = (int)c->tubelet_size;
+    g.ph = (int)c->patch_h;
+    g.pw = (int)c->patch_w;
+    if (dtype == SC_DTYPE_F32)
+        patch_gather_kernel<float><<<grid1d(rows * K, 256), 256, 0, st>>>(
+            static_cast<const float*>(input), reinterpret_cast<const int4*>(coords), rows, g, static_cast<float*>(cols));
+    else
+        patch_gather_kernel<__nv_bfloat16><<<grid1d(rows * K, 256), 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(input), reinterpret_cast<const int4*>(coords), rows, g,
+            static_cast<__nv_bfloat16*>(cols));
+    SC_CUDA_TRY(cudaGetLastError());
+    // projection: a 1x1x1 conv over the identity rows, weight [Cout, 1, 1, 1, K]
+    sc_conv_config cc;
+    memset(&cc, 0, sizeof cc);
+    cc.in_channels = K;
+    cc.out_channels = c->out_channels;
+    cc.kernel_d = cc.kernel_h = cc.kernel_w = 1;
+    cc.in_channels_per_group = K;
+    cc.out_channels_per_group = c->out_channels;
+    cc.groups = 1;
+    for (int j = 0; j < 3; ++j) {
+        cc.axis_order[j] = j;
+        cc.axis_sign[j] = 1;
+    }
+    sc_epilogue e;
+    memset(&e, 0, sizeof e);
+    e.residual_repeat = 1;
+    return sc_subm_conv_forward(&cc, dtype, cols, rows, ident, rows, weight, bias, &e, out, stream);
+}
+
+int sc_subdiv_head(sc_dtype dtype, const void* feats, int64_t n, int64_t channels, const void* weight,
+                   const float* bias, float threshold, const float* h_child_thresholds, int center,
+                   float* logits, uint8_t* mask, void* stream) {
+    if (n < 0 || channels <= 0) return fail(SC_ERR_INVALID, "subdivision head: invalid sizes");
+    if (n == 0) return SC_OK;
+    if (!feats || !weight || !mask) return fail(SC_ERR_INVALID, "subdivision head: null pointer");
+    if (dtype != SC_DTYPE_F32 && dtype != SC_DTYPE_BF16) return fail(SC_ERR_INVALID, "subdivision head: bad dtype");
+    SubdivThresholds thr;
+    for (int c = 0; c < 8; ++c) {
+        const float ch = h_child_thresholds ? h_child_thresholds[c] : NAN;
+        thr.t[c] = std::isfinite(ch) ? ch : threshold;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t threads = n * 32;
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    if (dtype == SC_DTYPE_F32)
+        subdiv_head_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(feats), n, (int)channels,
+                                                         static_cast<const float*>(weight), bias, thr, center,
+                                                         logits, mask);
+    else
+        subdiv_head_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(feats), n, (int)channels, static_cast<const __nv_bfloat16*>(weight),
+            bias, thr, center, logits, mask);
+    SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
 }
 

@@ -30,7 +30,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib
-from ._lib import DTYPE_BF16, DTYPE_F32, ScConvConfig, ScEpilogue, SparseConvError, check, lib
+from ._lib import DTYPE_BF16, DTYPE_F32, ScConvConfig, ScEpilogue, ScPatchify3dConfig, SparseConvError, check, lib
 
 INVALID_NEIGHBOR_ROW = -1
 
@@ -386,6 +386,36 @@ def cast(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return y
 
 
+def subdivision_child_thresholds(threshold: float = 0.0, child_thresholds=None) -> list:
+    """Per-child thresholds: a finite child threshold overrides the shared one
+    (decoder_subdivision_child_thresholds, sparse_decoder_wgpu_ops.rs:1813-1822)."""
+    import math
+    ct = list(child_thresholds) if child_thresholds is not None else [float("nan")] * 8
+    return [c if math.isfinite(c) else threshold for c in ct]
+
+
+def subdivision_head(feats: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                     threshold: float = 0.0, child_thresholds=None, center: bool = False,
+                     return_logits: bool = True):
+    """to_subdiv logits [N, 8] (linear C -> 8, fp32 accumulate; optional
+    centring on the row mean, sparse_decoder_runtime_impl.rs:852-880) and the
+    child mask [N, 8] uint8 = logits > per-child threshold
+    (subdivision_active_indices_wgpu_async, sparse_decoder_wgpu_ops.rs:928-992).
+    ``weight`` is [8, C] in feats' dtype, ``bias`` fp32."""
+    _require_cuda("feats", feats)
+    if feats.dim() != 2 or weight.shape != (8, feats.shape[1]) or weight.dtype != feats.dtype:
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"decoder subdivision logits tensor must have 8 columns (weight {tuple(weight.shape)})")
+    n = feats.shape[0]
+    logits = torch.empty((n, 8), dtype=torch.float32, device=feats.device) if return_logits else None
+    mask = torch.empty((n, 8), dtype=torch.uint8, device=feats.device)
+    thr = (ctypes.c_float * 8)(*subdivision_child_thresholds(threshold, child_thresholds))
+    check(lib().sc_subdiv_head(_DT[feats.dtype], _ptr(feats), n, feats.shape[1], _ptr(weight.contiguous()),
+                               _ptr(bias), ctypes.c_float(threshold), thr, int(center),
+                               _ptr(logits) if logits is not None else None, _ptr(mask), _stream(feats)))
+    return logits, mask
+
+
 def subdivide(parent_coords: torch.Tensor, mask: torch.Tensor, parent_channels: int):
     """Channel-to-space child expansion.  Returns (child_row [Np, 8] int32,
     child_coords [Nc, 4] int32, skip_offset [Nc] int64)."""
@@ -404,3 +434,56 @@ def subdivide(parent_coords: torch.Tensor, mask: torch.Tensor, parent_channels: 
                              _ptr(coords), _ptr(skip), ctypes.byref(nc), _stream(parent_coords)))
     k = nc.value
     return child_row, coords[:k].contiguous(), skip[:k].contiguous()
+
+
+@dataclass(frozen=True)
+class SparsePatchify3dConfig:
+    """Mirror of burn_flex_gmm's SparsePatchify3dConfig (src/lib.rs:26-35)."""
+    in_channels: int
+    out_channels: int
+    frames: int
+    height: int
+    width: int
+    tubelet_size: int
+    patch_h: int
+    patch_w: int
+
+    def c(self) -> ScPatchify3dConfig:
+        return ScPatchify3dConfig(self.in_channels, self.out_channels, self.frames, self.height, self.width,
+                                  self.tubelet_size, self.patch_h, self.patch_w)
+
+    def inner_len(self) -> int:
+        return self.in_channels * self.tubelet_size * self.patch_h * self.patch_w
+
+
+def sparse_patchify3d_forward(config: SparsePatchify3dConfig, input: torch.Tensor, coords: torch.Tensor,
+                              weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """Patch embedding at the listed patches (sparse_patchify3d_forward_flex,
+    burn_flex_gmm src/lib.rs:133-240).  ``input`` [B, Cin, T, H, W] (or any
+    contiguous tensor of B * Cin*T*H*W elements), ``coords`` [rows, 4] int32
+    (batch, tubelet, patch_row, patch_col), ``weight`` [Cout, Cin, tubelet,
+    patch_h, patch_w] in the input's dtype, ``bias`` [Cout] fp32.  Returns
+    [rows, Cout].  A coordinate outside the grid raises the device fault word
+    (the reference's CPU path returns an error) and yields the bias row."""
+    for name, t in (("input", input), ("coords", coords), ("weight", weight), ("bias", bias)):
+        _require_cuda(name, t)
+    if input.dtype not in _DT or weight.dtype != input.dtype:
+        raise SparseConvError(_lib.SC_ERR_INVALID, "sparse patchify input and weight must share an F32 or BF16 dtype")
+    if bias.shape[0] != config.out_channels:
+        raise SparseConvError(_lib.SC_ERR_INVALID, f"sparse patchify bias len mismatch: got {bias.shape[0]} "
+                                                   f"expected {config.out_channels}")
+    if weight.numel() != config.out_channels * config.inner_len():
+        raise SparseConvError(_lib.SC_ERR_INVALID, f"sparse patchify weight len mismatch: got {weight.numel()} "
+                                                   f"expected {config.out_channels * config.inner_len()}")
+    if coords.dtype != torch.int32 or coords.dim() != 2 or coords.shape[1] != 4:
+        raise SparseConvError(_lib.SC_ERR_INVALID, "sparse patchify coords must be [rows, 4] int32")
+    rows = coords.shape[0]
+    out = torch.empty((rows, config.out_channels), dtype=input.dtype, device=input.device)
+    c = config.c()
+    nbytes = ctypes.c_size_t(0)
+    check(lib().sc_patchify3d_scratch_bytes(ctypes.byref(c), rows, _DT[input.dtype], ctypes.byref(nbytes)))
+    scratch = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=input.device)
+    check(lib().sc_patchify3d_forward(ctypes.byref(c), _DT[input.dtype], _ptr(input.contiguous()), input.numel(),
+                                      _ptr(coords.contiguous()), rows, _ptr(weight.contiguous()), _ptr(bias),
+                                      _ptr(scratch), int(nbytes.value), _ptr(out), _stream(input)))
+    return out

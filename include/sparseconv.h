@@ -211,6 +211,39 @@ int sc_subdivide(const int32_t* d_parent_coords, const uint8_t* d_mask, int64_t 
                  int64_t* d_skip_offset /* [<= 8*n_parent] */, int64_t* h_children,
                  void* stream);
 
+/* ---- subdivision head (decoder upsample without a guide) -----------------
+ * logits[n, 8] = feats[n, C] @ weight[8, C]^T + bias (the to_subdiv linear
+ * layer; weight in feats' dtype, bias fp32, fp32 accumulate), optionally
+ * centred on each row's mean, and mask[n, 8] = logits > threshold[c], where
+ * threshold[c] = h_child_thresholds[c] when finite, else `threshold`
+ * (h_child_thresholds may be NULL).  Replaces burn_trellis
+ * sparse_decoder_runtime_impl.rs:852-890 (to_subdiv + centring) and the
+ * threshold of subdivision_active_indices_wgpu_async,
+ * sparse_decoder_wgpu_ops.rs:928-992 / :1813-1822.  d_logits may be NULL.
+ * The mask feeds sc_subdivide. */
+int sc_subdiv_head(sc_dtype dtype, const void* d_feats, int64_t n, int64_t channels, const void* d_weight,
+                   const float* d_bias, float threshold, const float* h_child_thresholds, int center,
+                   float* d_logits, uint8_t* d_mask, void* stream);
+
+/* ---- sparse 3-D patchify (patch embedding at listed patches) --------------
+ * out[r, :] = bias + W · patch(r) with patch(r) the input block
+ * [c, t0 + dt, y0 + py, x0 + px] (t0 = tubelet * tubelet_size, y0 = patch_row *
+ * patch_h, x0 = patch_col * patch_w) flattened in (c, dt, py, px) order, for
+ * coords[r] = (batch, tubelet, patch_row, patch_col).  Input [B, Cin, T, H, W],
+ * weight [Cout, Cin, tubelet, patch_h, patch_w] and output share `dtype`; bias
+ * fp32.  Replaces burn_flex_gmm sparse_patchify3d_forward_flex (lib.rs:133-240,
+ * validation :558-696).  The gather writes an im2col block into d_scratch
+ * (sc_patchify3d_scratch_bytes) and the projection runs on the conv path (a
+ * 1x1x1 conv over the identity rows).  Coordinates outside the grid raise the
+ * device fault word and give bias-only rows. */
+typedef struct sc_patchify3d_config {
+    int64_t in_channels, out_channels, frames, height, width, tubelet_size, patch_h, patch_w;
+} sc_patchify3d_config;
+int sc_patchify3d_scratch_bytes(const sc_patchify3d_config* cfg, int64_t rows, sc_dtype dtype, size_t* h_bytes);
+int sc_patchify3d_forward(const sc_patchify3d_config* cfg, sc_dtype dtype, const void* d_input,
+                          int64_t input_elems, const int32_t* d_coords, int64_t rows, const void* d_weight,
+                          const float* d_bias, void* d_scratch, size_t scratch_bytes, void* d_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

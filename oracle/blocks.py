@@ -58,6 +58,20 @@ def linear(x, w, b, bf16: bool, threads: int = 8):
     return subm_conv_flex(cfg, _q(w, bf16).reshape(cout, 1, 1, 1, cin), b, _q(x, bf16), ident, threads=threads)
 
 
+def subdivision_head(x, w, b, threshold: float = 0.0, child_thresholds=None, center: bool = False,
+                     bf16: bool = False, threads: int = 8):
+    """to_subdiv logits [N, 8] = linear(x) (sparse_decoder_runtime_impl.rs:852-873), optionally
+    minus the row mean (:875-877), and the child mask logits > threshold[c] with
+    a finite per-child threshold overriding the shared one
+    (sparse_decoder_wgpu_ops.rs:986-991, :1813-1822)."""
+    logits = linear(x, w, b, bf16, threads).astype(np.float32)
+    if center:
+        logits = logits - logits.mean(axis=1, keepdims=True)
+    ct = [float("nan")] * 8 if child_thresholds is None else list(child_thresholds)
+    thr = np.array([c if np.isfinite(c) else threshold for c in ct], np.float32)
+    return logits, (logits > thr[None, :]).astype(np.uint8)
+
+
 def convnext_block(x, nbr, p, bf16: bool, threads: int = 8):
     """One ConvNeXt decoder block; returns the fp32 (unrounded) output."""
     x = _q(x, bf16)

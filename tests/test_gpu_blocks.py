@@ -147,3 +147,90 @@ def test_convnext_stack(cuda_device, c, hidden, nblocks):
         ref = OB.convnext_stack(x, nbr.cpu().numpy(), params, bf16=True)
         assert rel_l2(got, ref) <= 1e-2, rel_l2(got, ref)
     assert_no_fault()
+
+
+@pytest.mark.parametrize("c,dtype,center,child", [(256, torch.bfloat16, False, None),
+                                                  (96, torch.float32, True, None),
+                                                  (768, torch.bfloat16, False, [0.1, float("nan"), -0.2, 0, 0, 0, 0, 0.3])])
+def test_subdivision_head(cuda_device, c, dtype, center, child):
+    """to_subdiv linear + centring + per-child threshold (sparse_decoder_runtime_impl.rs:852-890,
+    sparse_decoder_wgpu_ops.rs:928-992, :1813-1822)."""
+    rng = np.random.default_rng(c)
+    n = 3000
+    x = rng.standard_normal((n, c)).astype(np.float32)
+    w = (0.1 * rng.standard_normal((8, c))).astype(np.float32)
+    b = (0.1 * rng.standard_normal(8)).astype(np.float32)
+    logits, mask = F.subdivision_head(to_dev(x, dtype), to_dev(w, dtype), to_dev(b), 0.05, child, center)
+    rl, rm = OB.subdivision_head(x, w, b, 0.05, child, center, bf16=dtype == torch.bfloat16)
+    got_l = logits.cpu().numpy()
+    assert rel_l2(got_l, rl) <= 1e-5, rel_l2(got_l, rl)
+    thr = np.array(F.subdivision_child_thresholds(0.05, child), np.float32)
+    near = np.abs(rl - thr[None, :]) < 1e-4 * np.abs(rl).max()
+    diff = mask.cpu().numpy() != rm
+    assert not (diff & ~near).any()
+    assert_no_fault()
+
+
+def test_c2s_block_predicted_mask(cuda_device):
+    """C2S upsample with the child mask predicted by to_subdiv (no guide)."""
+    coords = shell(grid=24, r=8.0)
+    n = coords.shape[0]
+    cin, cout = 192, 96
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((n, cin)).astype(np.float32)
+    p = synth.c2s_params(rng, cin, cout)
+    w_sub = (0.1 * rng.standard_normal((8, cin))).astype(np.float32)
+    b_sub = np.zeros(8, np.float32)
+    xd = to_dev(x, torch.bfloat16)
+    _, mask = F.subdivision_head(xd, to_dev(w_sub, torch.bfloat16), to_dev(b_sub))
+    blk = blocks.C2SUpsampleBlock(blocks.C2SParams.from_numpy(p, dev()))
+    cc, y, _ = blk.forward(to_dev(coords), xd, mask)
+    m = mask.cpu().numpy()
+    assert 0 < m.sum() < m.size
+    rc, ry = OB.c2s_block(coords, x, m, p, bf16=True)
+    np.testing.assert_array_equal(cc.cpu().numpy(), rc.astype(np.int32))
+    assert rel_l2(y.float().cpu().numpy(), ry) <= 1e-2
+    assert_no_fault()
+
+
+@pytest.mark.parametrize("cin,cout,tb,ph,pw,dtype,tol", [(4, 40, 2, 2, 2, torch.float32, 1e-5),
+                                                         (16, 64, 1, 2, 2, torch.bfloat16, 1e-2),
+                                                         (8, 128, 2, 2, 2, torch.bfloat16, 1e-2)])
+def test_sparse_patchify3d(cuda_device, cin, cout, tb, ph, pw, dtype, tol):
+    """Sparse patch embedding (burn_flex_gmm lib.rs:133-240) vs the numpy oracle."""
+    from oracle import patchify as OP
+    cfg = F.SparsePatchify3dConfig(cin, cout, 8, 16, 12, tb, ph, pw)
+    d = dict(cfg.__dict__)
+    rng = np.random.default_rng(cin + cout)
+    x = rng.standard_normal((2, cin, 8, 16, 12)).astype(np.float32)
+    w = (0.1 * rng.standard_normal((cout, cin, tb, ph, pw))).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    gt, gh, gw = 8 // tb, 16 // ph, 12 // pw
+    allc = np.array([[bb, t, y, xx] for bb in range(2) for t in range(gt) for y in range(gh) for xx in range(gw)],
+                    np.int32)
+    coords = allc[rng.random(len(allc)) < 0.3]
+    got = F.sparse_patchify3d_forward(cfg, to_dev(x, dtype), to_dev(coords), to_dev(w, dtype), to_dev(b))
+    xr, wr = (oracle.bf16_round(x), oracle.bf16_round(w)) if dtype == torch.bfloat16 else (x, w)
+    ref = OP.sparse_patchify3d_forward(d, wr, b, coords, xr)
+    if dtype == torch.bfloat16:
+        ref = oracle.bf16_round(ref)
+    assert rel_l2(got.float().cpu().numpy(), ref) <= tol, rel_l2(got.float().cpu().numpy(), ref)
+    assert_no_fault()
+
+
+def test_sparse_patchify3d_bad_coords(cuda_device):
+    """A coordinate outside the grid: the gather's own check raises the fault word, the row is bias only."""
+    from bevy_synth_b200 import _lib
+    cfg = F.SparsePatchify3dConfig(2, 32, 2, 4, 4, 1, 2, 2)
+    x = to_dev(np.ones((1, 2, 2, 4, 4), np.float32))
+    w = to_dev(np.ones((32, 2, 1, 2, 2), np.float32))
+    b = to_dev(np.arange(32, dtype=np.float32))
+    coords = to_dev(np.array([[0, 0, 0, 0], [0, 5, 0, 0]], np.int32))
+    out = F.sparse_patchify3d_forward(cfg, x, coords, w, b).cpu().numpy()
+    torch.cuda.synchronize()
+    assert _lib.device_fault() != 0
+    np.testing.assert_allclose(out[0], np.arange(32) + 8.0)
+    np.testing.assert_allclose(out[1], np.arange(32))
+    with pytest.raises(F.SparseConvError, match="frames must be divisible by tubelet_size"):
+        F.sparse_patchify3d_forward(F.SparsePatchify3dConfig(2, 32, 3, 4, 4, 2, 2, 2), x, coords,
+                                    to_dev(np.ones((32, 2, 2, 2, 2), np.float32)), b)
