@@ -234,3 +234,40 @@ def test_sparse_patchify3d_bad_coords(cuda_device):
     with pytest.raises(F.SparseConvError, match="frames must be divisible by tubelet_size"):
         F.sparse_patchify3d_forward(F.SparsePatchify3dConfig(2, 32, 3, 4, 4, 2, 2, 2), x, coords,
                                     to_dev(np.ones((32, 2, 2, 2, 2), np.float32)), b)
+
+
+def test_load_decoder_stage_from_safetensors(cuda_device, tmp_path):
+    """Weight ingestion (sparse_decoder_loading.rs) -> ConvNeXt stage and C2S block, same results as
+    building them from the arrays directly (f32 payloads rounded to bf16 by sc_cast; bf16 payloads copied)."""
+    from bevy_synth_b200 import weights as Wt
+    c, hidden, cout = 64, 256, 32
+    rng = np.random.default_rng(5)
+    blocks_np = [synth.convnext_params(rng, c, hidden) for _ in range(2)]
+    c2s = synth.c2s_params(rng, c, cout)
+    w_sub = (0.1 * rng.standard_normal((8, c))).astype(np.float32)
+    t = {}
+    for i, p in enumerate(blocks_np):
+        pre = f"blocks.1.{i}"
+        t.update({f"{pre}.conv.weight": p["w"], f"{pre}.conv.bias": p["b"], f"{pre}.norm.weight": p["norm_g"],
+                  f"{pre}.norm.bias": p["norm_b"], f"{pre}.mlp.0.weight": p["w0"], f"{pre}.mlp.0.bias": p["b0"],
+                  f"{pre}.mlp.2.weight": p["w2"], f"{pre}.mlp.2.bias": p["b2"]})
+    pre = "blocks.1.2"
+    t.update({f"{pre}.norm1.weight": c2s["ln1_g"], f"{pre}.norm1.bias": c2s["ln1_b"],
+              f"{pre}.conv1.weight": c2s["w1"], f"{pre}.conv1.bias": c2s["b1"],
+              f"{pre}.conv2.weight": c2s["w2"], f"{pre}.conv2.bias": c2s["b2"],
+              f"{pre}.to_subdiv.weight": w_sub, f"{pre}.to_subdiv.bias": np.zeros(8, np.float32)})
+    path = tmp_path / "decoder.safetensors"
+    Wt.write_safetensors(path, t, bf16=tuple(k for k in t if k.endswith("mlp.0.weight")))
+    st = Wt.read_safetensors(str(path))
+    stack = Wt.load_convnext_stage(st, 1, 2, c, dev())
+    direct = blocks.ConvNeXtStack([blocks.ConvNeXtParams.from_numpy(p, dev()) for p in blocks_np])
+    coords = shell()
+    x = to_dev(rng.standard_normal((coords.shape[0], c)).astype(np.float32), torch.bfloat16)
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(stack.cfg, to_dev(coords))
+    a = stack.forward(x, nbr)
+    b = direct.forward(x, nbr)
+    assert torch.equal(a, b)
+    blk = Wt.load_c2s_block(st, 1, 2, c, cout, dev())
+    cc, y, _ = blk.forward(to_dev(coords), a)  # children from the loaded to_subdiv head
+    assert cc.shape[0] > 0 and y.shape == (cc.shape[0], cout)
+    assert_no_fault()
