@@ -133,6 +133,7 @@ class C2SUpsampleBlock:
         self.cout = p.w2.shape[0]
         self.cfg1 = F.SparseSubmConvConfig.subm3(self.cin, 8 * self.cout)
         self.cfg2 = F.SparseSubmConvConfig.subm3(self.cout, self.cout)
+        self.group_children = True
 
     def forward(self, coords: torch.Tensor, x: torch.Tensor, mask: torch.Tensor | None = None, nbr_parent=None,
                 threshold: float = 0.0):
@@ -149,10 +150,13 @@ class C2SUpsampleBlock:
         n_child = child_coords.shape[0]
         if nbr_parent is None:
             nbr_parent = F.neighbor_rows_tensor_from_coords_tensor(self.cfg1, coords)
+        # parents grouped by their kept-children mask, then by tap mask: a tile whose
+        # parents keep none of a child block skips that block's MMAs (dry stage)
+        sched1 = F.neighbor_schedule(self.cfg1, nbr_parent, group_mask=mask) if self.group_children else None
         h_up = F.sparse_subm_conv_forward(
             self.cfg1, h, nbr_parent, p.w1, p.b1,
             F.Epilogue(layer_norm=True, ln_width=self.cout, ln_eps=C2S_LN_EPS, silu=True,
-                       out_row_map=child_row, out_row_map_cols=8),
+                       out_row_map=child_row, out_row_map_cols=8, schedule=sched1),
             out_rows=n_child)
         nbr_child = F.neighbor_rows_tensor_from_coords_tensor(self.cfg2, child_coords)
         rep = self.cout // (self.cin // 8)

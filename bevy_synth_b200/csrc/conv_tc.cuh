@@ -511,7 +511,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 break;
             }
             if (fast_map && nt >= 0) load_my_map(nt);
-            const int n_steps = __popc(mask) * n_chunks;
+            // A scatter conv (C2S conv1: column tile = child block) whose tile keeps no child of
+            // this block writes nothing: run it as one "dry" stage (no copies; the MMAs read stale
+            // shared memory into an accumulator whose rows are all discarded).
+            bool dry = false;
+            if (!PAIR && p.gather4 == 0 && p.row_map != nullptr && p.map_cols > 1) {
+                const int wb = p.cout / p.map_cols;
+                const int blk = n0 / wb;
+                bool kept = false;
+                for (int i = lane; i < TILE_ROWS; i += 32) {
+                    const int64_t pos = tile_row0 + i;
+                    if (pos < p.n_rows) {
+                        const int64_t row = ordered_row(p.row_order, pos, p.n_rows);
+                        if (row >= 0 && __ldg(p.row_map + row * p.map_cols + blk) >= 0) kept = true;
+                    }
+                }
+                dry = !__any_sync(0xffffffffu, kept);
+            }
+            const int chunks = dry ? 1 : n_chunks;
+            if (dry) mask = mask & (~mask + 1u);  // the lowest valid tap only
+            const int n_steps = __popc(mask) * chunks;
             int step = 0;
             for (uint32_t m = mask; m && ok; m &= m - 1) {
                 const int k = __ffs(m) - 1;
@@ -527,10 +546,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                     for (int i = 0; i < GROUPS; ++i) src[i] = my_nbr[(i * 4 + sub) * K + k];
                 }
-                for (int ch = 0; ch < n_chunks; ++ch, ++step) {
+                for (int ch = 0; ch < chunks; ++ch, ++step) {
                     if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u))) {
                         ok = false;
                         break;
+                    }
+                    if (dry) {
+                        // every arrival the stage expects, no copies
+                        if (pw == 0 && lane == 0) {
+                            if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
+                            stage_flags[s] = 2u;
+                            mbar_arrive(&full[s]);
+                        }
+                        mbar_arrive(&full[s]);
+                        if (++s == S) {
+                            s = 0;
+                            ph ^= 1u;
+                        }
+                        continue;
                     }
                     if (G4) {
                         // A by TMA row gathers; one expect_tx (leader / single CTA) covers every byte

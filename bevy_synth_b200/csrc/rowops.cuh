@@ -83,6 +83,24 @@ __global__ void row_mask_key_kernel(const int32_t* __restrict__ nbr, int64_t n, 
     vals[r] = (int32_t)r;
 }
 
+// 64-bit key: the row's group (8 bits from a [n, 8] 0/1 mask, bit c = column
+// c) above its 32-bit valid-tap key, so a stable sort groups rows by group
+// first and by tap mask within a group.
+__global__ void row_group_key_kernel(const int32_t* __restrict__ nbr, int64_t n, const TapRank tr,
+                                     const uint8_t* __restrict__ group_mask8, uint64_t* __restrict__ keys,
+                                     int32_t* __restrict__ vals) {
+    int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n) return;
+    uint32_t key = 0;
+    for (int k = 0; k < tr.k; ++k)
+        if (__ldg(nbr + r * tr.k + k) >= 0) key |= 1u << (tr.k - 1 - tr.rank_of_tap[k]);
+    uint32_t g = 0;
+    if (group_mask8)
+        for (int c = 0; c < 8; ++c) g |= (__ldg(group_mask8 + r * 8 + c) ? 1u : 0u) << c;
+    keys[r] = ((uint64_t)g << 32) | key;
+    vals[r] = (int32_t)r;
+}
+
 // dst[i, :] = src[idx[i], :] for rows of `row_units` 16-byte units (halo packing).
 __global__ void gather_rows_kernel(const uint4* __restrict__ src, int64_t row_units,
                                    const int32_t* __restrict__ idx, int64_t n, int64_t n_src,

@@ -579,6 +579,60 @@ int sc_neighbor_schedule(const sc_conv_config* cfg, const int32_t* nbr, int64_t 
     return SC_OK;
 }
 
+static size_t order64_cub_bytes(int64_t n) {
+    size_t b = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, b, (const uint64_t*)nullptr, (uint64_t*)nullptr,
+                                    (const int32_t*)nullptr, (int32_t*)nullptr, (int)n, 0, 40);
+    return b;
+}
+
+int sc_neighbor_schedule_grouped_scratch_bytes(int64_t n, size_t* bytes) {
+    if (n < 0 || !bytes) return fail(SC_ERR_INVALID, "invalid row order scratch query");
+    *bytes = 2 * align256((size_t)n * 8) + align256((size_t)n * 4) + order64_cub_bytes(n) + 256;
+    return SC_OK;
+}
+
+int sc_neighbor_schedule_grouped(const sc_conv_config* cfg, const int32_t* nbr, int64_t n,
+                                 const uint8_t* group_mask8, void* scratch, size_t scratch_bytes, int32_t* order,
+                                 int32_t* nbr_ordered, void* stream) {
+    if (int rc = validate_config(cfg)) return rc;
+    const int64_t K = kernel_rows_of(cfg);
+    if (K > 32) return fail(SC_ERR_UNSUPPORTED, "row order supports at most 32 kernel offsets");
+    if (n < 0) return fail(SC_ERR_INVALID, "negative row count");
+    if (n == 0) return SC_OK;
+    if (n > 0x7fffffffLL) return fail(SC_ERR_UNSUPPORTED, "too many rows");
+    size_t need = 0;
+    sc_neighbor_schedule_grouped_scratch_bytes(n, &need);
+    if (!scratch || scratch_bytes < need)
+        return fail(SC_ERR_CAPACITY, "row order scratch too small: need " + std::to_string(need) + " bytes");
+    if (!nbr || !order) return fail(SC_ERR_INVALID, "null pointer");
+    int32_t off[3 * 32];
+    kernel_offsets_of(cfg, off);
+    TapRank tr;
+    tr.k = (int32_t)K;
+    int idx[32];
+    for (int i = 0; i < K; ++i) idx[i] = i;
+    auto l1 = [&](int i) { return std::abs(off[3 * i]) + std::abs(off[3 * i + 1]) + std::abs(off[3 * i + 2]); };
+    std::stable_sort(idx, idx + K, [&](int a, int b) { return l1(a) > l1(b); });
+    for (int r = 0; r < K; ++r) tr.rank_of_tap[idx[r]] = (int8_t)r;
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    uint64_t* keys_in = reinterpret_cast<uint64_t*>(base);
+    uint64_t* keys_out = reinterpret_cast<uint64_t*>(base + align256((size_t)n * 8));
+    int32_t* vals_in = reinterpret_cast<int32_t*>(base + 2 * align256((size_t)n * 8));
+    void* tmp = base + 2 * align256((size_t)n * 8) + align256((size_t)n * 4);
+    size_t tmp_bytes = order64_cub_bytes(n);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    row_group_key_kernel<<<grid1d(n, 256), 256, 0, st>>>(nbr, n, tr, group_mask8, keys_in, vals_in);
+    SC_CUDA_TRY(cudaGetLastError());
+    SC_CUDA_TRY(cub::DeviceRadixSort::SortPairs(tmp, tmp_bytes, keys_in, keys_out, vals_in, order, (int)n, 0,
+                                                32 + (group_mask8 ? 8 : 0), st));
+    if (nbr_ordered) {
+        permute_rows_kernel<<<grid1d(n * K, 256), 256, 0, st>>>(nbr, order, n, (int)K, nbr_ordered);
+        SC_CUDA_TRY(cudaGetLastError());
+    }
+    return SC_OK;
+}
+
 int sc_conv_uses_tensor_cores(const sc_conv_config* cfg, sc_dtype dtype, int32_t* flag) {
     if (int rc = validate_config(cfg)) return rc;
     if (!flag) return fail(SC_ERR_INVALID, "flag is null");

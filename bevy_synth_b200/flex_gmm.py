@@ -159,8 +159,14 @@ class ConvSchedule:
     nbr_ordered: torch.Tensor    # [N, K] int32 = nbr[order]
 
 
-def neighbor_schedule(config: SparseSubmConvConfig, neighbor_rows: torch.Tensor) -> ConvSchedule:
+def neighbor_schedule(config: SparseSubmConvConfig, neighbor_rows: torch.Tensor,
+                      group_mask: torch.Tensor | None = None) -> ConvSchedule:
+    """Conv schedule of a map (sc_neighbor_schedule).  With ``group_mask``
+    ([N, 8] uint8 0/1, e.g. a C2S conv1's kept-children mask) rows are grouped
+    by that mask first (sc_neighbor_schedule_grouped)."""
     _require_cuda("neighbor_rows", neighbor_rows)
+    if group_mask is not None:
+        return _neighbor_schedule_grouped(config, neighbor_rows, group_mask)
     n = neighbor_rows.shape[0]
     b = ctypes.c_size_t(0)
     check(lib().sc_neighbor_schedule_scratch_bytes(n, ctypes.byref(b)))
@@ -170,6 +176,22 @@ def neighbor_schedule(config: SparseSubmConvConfig, neighbor_rows: torch.Tensor)
     c = config.c()
     check(lib().sc_neighbor_schedule(ctypes.byref(c), _ptr(neighbor_rows), n, _ptr(scratch), b.value, _ptr(order),
                                      _ptr(ordered), _stream(neighbor_rows)))
+    return ConvSchedule(order, ordered)
+
+
+def _neighbor_schedule_grouped(config, neighbor_rows, group_mask) -> ConvSchedule:
+    n = neighbor_rows.shape[0]
+    if group_mask.shape != (n, 8) or group_mask.dtype != torch.uint8:
+        raise SparseConvError(_lib.SC_ERR_INVALID, "schedule group mask must be [rows, 8] uint8")
+    b = ctypes.c_size_t(0)
+    check(lib().sc_neighbor_schedule_grouped_scratch_bytes(n, ctypes.byref(b)))
+    scratch = torch.empty(max(b.value, 1), dtype=torch.uint8, device=neighbor_rows.device)
+    order = torch.empty(n, dtype=torch.int32, device=neighbor_rows.device)
+    ordered = torch.empty_like(neighbor_rows)
+    c = config.c()
+    check(lib().sc_neighbor_schedule_grouped(ctypes.byref(c), _ptr(neighbor_rows), n, _ptr(group_mask.contiguous()),
+                                             _ptr(scratch), b.value, _ptr(order), _ptr(ordered),
+                                             _stream(neighbor_rows)))
     return ConvSchedule(order, ordered)
 
 

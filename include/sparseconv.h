@@ -162,6 +162,16 @@ int sc_neighbor_schedule(const sc_conv_config* cfg, const int32_t* d_neighbor_ro
                          void* d_scratch, size_t scratch_bytes, int32_t* d_row_order,
                          int32_t* d_neighbor_rows_ordered, void* stream);
 
+/* The same schedule with a per-row group above the tap key: rows are sorted
+ * by group first (8 bits from d_group_mask8 [n_rows, 8] 0/1, bit c = column
+ * c; nullable), then by their tap mask.  For the decoder's channel-to-space
+ * conv1 the group is the kept-children mask: a tile of parents that keeps no
+ * child in some column block then skips that block (see sc_epilogue). */
+int sc_neighbor_schedule_grouped_scratch_bytes(int64_t n_rows, size_t* h_bytes);
+int sc_neighbor_schedule_grouped(const sc_conv_config* cfg, const int32_t* d_neighbor_rows, int64_t n_rows,
+                                 const uint8_t* d_group_mask8, void* d_scratch, size_t scratch_bytes,
+                                 int32_t* d_row_order, int32_t* d_neighbor_rows_ordered, void* stream);
+
 /* ---- convolution ----------------------------------------------------------
  * out[n_rows, Cout] = bias + sum_k sum_c in[nbr[r,k], c] * W[o,k,c]  (+ epilogue)
  * d_input [n_in, Cin], d_neighbor_rows [n_rows, K] (n_rows <= n_in is not

@@ -271,3 +271,29 @@ def test_load_decoder_stage_from_safetensors(cuda_device, tmp_path):
     cc, y, _ = blk.forward(to_dev(coords), a)  # children from the loaded to_subdiv head
     assert cc.shape[0] > 0 and y.shape == (cc.shape[0], cout)
     assert_no_fault()
+
+
+def test_c2s_grouped_schedule(cuda_device):
+    """Parents grouped by kept-children mask (sc_neighbor_schedule_grouped): the order is a permutation
+    sorted by group, and conv1's dry-stage skipping leaves the block's output bit-identical."""
+    coords = shell(grid=28, r=10.0)
+    n = coords.shape[0]
+    cin, cout = 128, 64
+    rng = np.random.default_rng(4)
+    x = to_dev(rng.standard_normal((n, cin)).astype(np.float32), torch.bfloat16)
+    p = synth.c2s_params(rng, cin, cout)
+    mask = to_dev(synth.child_mask(3, n, 0.3))
+    blk = blocks.C2SUpsampleBlock(blocks.C2SParams.from_numpy(p, dev()))
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(blk.cfg1, to_dev(coords))
+    sched = F.neighbor_schedule(blk.cfg1, nbr, group_mask=mask)
+    order = sched.order.cpu().numpy()
+    assert np.array_equal(np.sort(order), np.arange(n))
+    g = (mask.cpu().numpy().astype(np.int64) << np.arange(8)).sum(1)
+    assert np.all(np.diff(g[order]) >= 0)
+    np.testing.assert_array_equal(sched.nbr_ordered.cpu().numpy(), nbr.cpu().numpy()[order])
+    blk.group_children = True
+    c1, y1, _ = blk.forward(to_dev(coords), x, mask)
+    blk.group_children = False
+    c0, y0, _ = blk.forward(to_dev(coords), x, mask)
+    assert torch.equal(c1, c0) and torch.equal(y1, y0)
+    assert_no_fault()
