@@ -86,6 +86,7 @@ struct TcParams {
     int grid_y;   // column tiles per row tile
     int64_t n_tiles;
     int dynamic;  // 1: one CTA per tile, CTAs claim unlaunched tiles by cluster launch control
+    int tma_epi;  // 1: staging is TMA-swizzled (64 columns); outputs by scatter4 (omap, o2map), dense residual by gather4 (rmap)
     int gather4;  // 1: A rows gathered by TMA (tile::gather4 on `amap`) instead of cp.async; 2: half of them
     int stg_cols; // epilogue staging width: a multiple of 32 dividing tile_n, <= TC_STG_COLS
     // epilogue
@@ -139,10 +140,17 @@ __device__ __forceinline__ void load_bf16x8(const uint8_t* src, float* v) {
 // Epilogue staging of one warp: 32 rows of `units` 16-byte units, padded by
 // one unit per row so that the owning thread's row writes and the warp's
 // row-wide reads are both free of bank conflicts.
+// A warp's staging buffer: 32 rows of `units` 16-byte chunks.  Padded rows
+// (one spare chunk per row) for per-row bulk copies; or, with swz (units ==
+// 8), dense 128-byte rows in the TMA 128B swizzle (chunk u of row r at
+// r*128 + ((u ^ (r & 7)) * 16), base 1024-aligned) for gather4 / scatter4.
 struct Staging {
     uint8_t* base;
     int units;
-    __device__ __forceinline__ uint8_t* at(int r, int u) const { return base + (r * (units + 1) + u) * 16; }
+    int swz;
+    __device__ __forceinline__ uint8_t* at(int r, int u) const {
+        return swz ? base + r * 128 + ((u ^ (r & 7)) << 4) : base + (r * (units + 1) + u) * 16;
+    }
 };
 
 // Lane's staged row -> global row orow (< 0: skipped), columns [col0,
@@ -158,7 +166,10 @@ __device__ __forceinline__ void store_staged_rows(const Staging& st, int64_t oro
 }
 
 // The staging buffer may be written again: this lane's bulk stores have read it.
-__device__ __forceinline__ void stg_reuse() { bulk_wait_read_all(); }
+__device__ __forceinline__ void stg_reuse() {
+    bulk_wait_read_all();
+    __syncwarp();  // lanes whose copies read other lanes' staged rows have waited too
+}
 
 // Global row rrow (per lane = row; < 0 gives zeros) -> the lane's staged row,
 // by bulk copy completing on the warp's barrier `bar` (phase `ph`, flipped).
@@ -173,6 +184,54 @@ __device__ __forceinline__ bool load_staged_rows(const Staging& st, int64_t rrow
     } else {
         for (int u = 0; u < st.units; ++u) *reinterpret_cast<uint4*>(st.at(lane, u)) = make_uint4(0, 0, 0, 0);
     }
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, ph));
+    ph ^= 1u;
+    return ok;
+}
+
+// Swizzled staging -> global rows orow (per lane = row) by TMA scatter4:
+// lanes 0-7 each write four rows.  A group of four with a row to skip is
+// written by the warp with 16-byte stores instead.
+__device__ __forceinline__ void store_staged_tma(const Staging& st, int64_t orow, const CUtensorMap* map,
+                                                 __nv_bfloat16* dst, int64_t ld, int col0, int lane) {
+    fence_proxy_async_smem();  // this lane's staging writes -> the scatter's reads
+    __syncwarp();
+    const int g = lane & 7;
+    int y[4];
+    bool full = true;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t o = __shfl_sync(0xffffffffu, orow, 4 * g + i);
+        y[i] = (int)o;
+        full = full && o >= 0;
+    }
+    // row 4g starts at base + 4g * 128 (the swizzle permutes chunks within rows, base is 1024-aligned)
+    if (lane < 8 && full) tma_scatter4(map, smem_u32(st.base + 4 * g * 128), col0, y[0], y[1], y[2], y[3]);
+    if (lane < 8) bulk_commit();
+    const unsigned partial = __ballot_sync(0xffffffffu, lane < 8 && !full);
+    for (unsigned m = partial; m; m &= m - 1) {
+        const int gg = __ffs(m) - 1;  // rows 4gg..4gg+3: one 16-byte chunk per lane
+        const int r = 4 * gg + (lane >> 3), u = lane & 7;
+        const int64_t o = __shfl_sync(0xffffffffu, orow, r);
+        if (o >= 0) *reinterpret_cast<uint4*>(dst + o * ld + col0 + u * 8) = *reinterpret_cast<const uint4*>(st.at(r, u));
+    }
+}
+
+// Global rows rrow (per lane = row; < 0 gives zeros) -> swizzled staging by
+// TMA gather4 (lanes 0-7, four rows each; rows < 0 read past the tensor's end,
+// which fills zeros), completing on the warp's barrier.
+__device__ __forceinline__ bool load_staged_tma(const Staging& st, int64_t rrow, const CUtensorMap* map, int col0,
+                                                int64_t n_rows_src, int lane, uint64_t* bar, uint32_t& ph) {
+    if (lane == 0) mbar_arrive_expect_tx(bar, 32u * 128u);
+    __syncwarp();
+    const int g = lane & 7;
+    int y[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t o = __shfl_sync(0xffffffffu, rrow, 4 * g + i);
+        y[i] = (int)(o >= 0 ? o : n_rows_src);
+    }
+    if (lane < 8) tma_gather4(smem_u32(st.base + 4 * g * 128), map, bar, col0, y[0], y[1], y[2], y[3]);
     const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, ph));
     ph ^= 1u;
     return ok;
@@ -200,7 +259,8 @@ __device__ __forceinline__ void add_param32(float (&v)[32], const float* p, bool
 template <bool PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
-                   const TcParams p) {
+                   const __grid_constant__ CUtensorMap omap, const __grid_constant__ CUtensorMap o2map,
+                   const __grid_constant__ CUtensorMap rmap, const TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -761,7 +821,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ====================================================== epilogue
         Staging st;
         st.units = stg_units;
-        st.base = stg_smem + warp * 32 * (stg_units + 1) * 16;
+        st.swz = p.tma_epi;
+        st.base = p.tma_epi ? stg_smem + warp * 32 * 128 : stg_smem + warp * 32 * (stg_units + 1) * 16;
         uint32_t res_ph = 0;  // phase of this warp's residual barrier
         const int t = tid;  // TMEM lane == tile row (of this CTA's half)
         const int W = p.ln_width;
@@ -820,7 +881,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (!multi) {
                 for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
                     stg_reuse();
-                    if (dense_res && !load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane, &res_bar[warp], res_ph))
+                    if (dense_res &&
+                        !(p.tma_epi ? load_staged_tma(st, row, &rmap, n0 + g0, p.n_rows, lane, &res_bar[warp], res_ph)
+                                    : load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane, &res_bar[warp], res_ph)))
                         *abort_flag = 1u;
                     for (int c = g0; c < g0 + stg_cols; c += 32) {
                         float v[32];
@@ -832,7 +895,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         stage_out(c, g0, v);
                     }
                     __syncwarp();
-                    store_staged_rows(st, orow, p.out, old, ocol0 + g0, lane);
+                    if (p.tma_epi)
+                        store_staged_tma(st, orow, &omap, p.out, old, ocol0 + g0, lane);
+                    else
+                        store_staged_rows(st, orow, p.out, old, ocol0 + g0, lane);
                     __syncwarp();
                 }
             } else {
@@ -840,7 +906,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 float sum[4] = {0.f, 0.f, 0.f, 0.f};  // <= 4 LayerNorm groups per tile
                 for (int g0 = 0; g0 < p.tile_n; g0 += stg_cols) {
                     stg_reuse();
-                    if (dense_res && !load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane, &res_bar[warp], res_ph))
+                    if (dense_res &&
+                        !(p.tma_epi ? load_staged_tma(st, row, &rmap, n0 + g0, p.n_rows, lane, &res_bar[warp], res_ph)
+                                    : load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane, &res_bar[warp], res_ph)))
                         *abort_flag = 1u;
                     for (int c = g0; c < g0 + stg_cols; c += 32) {
                         float v[32];
@@ -904,7 +972,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             stage_out(c, g0, v);
                         }
                         __syncwarp();
-                        store_staged_rows(st, orow, p.out, old, ocol0 + g0, lane);
+                        if (p.tma_epi)
+                            store_staged_tma(st, orow, &omap, p.out, old, ocol0 + g0, lane);
+                        else
+                            store_staged_rows(st, orow, p.out, old, ocol0 + g0, lane);
                         __syncwarp();
                     }
                 }
@@ -932,7 +1003,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         stage_out(c, g0, v);
                     }
                     __syncwarp();
-                    store_staged_rows(st, orow, dst, old, ocol0 + g0, lane);
+                    if (p.tma_epi)
+                        store_staged_tma(st, orow, p.out2 ? &o2map : &omap, dst, old, ocol0 + g0, lane);
+                    else
+                        store_staged_rows(st, orow, dst, old, ocol0 + g0, lane);
                     __syncwarp();
                 }
             }

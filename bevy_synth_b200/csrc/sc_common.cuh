@@ -300,6 +300,17 @@ __device__ __forceinline__ void tma_gather4_pair(uint32_t dst, const void* desc,
         : "memory");
 }
 
+// Row scatter: four consecutive box rows at src -> rows y0..y3 of a 2-D tensor
+// map, `box_x` columns from x (the map's swizzle applied), tracked by this
+// thread's bulk groups.  Every coordinate must be a row of the tensor.
+__device__ __forceinline__ void tma_scatter4(const void* desc, uint32_t src, int x, int y0, int y1, int y2, int y3) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.tile::scatter4.bulk_group"
+        " [%0, {%1, %2, %3, %4, %5}], [%6];" ::"l"(desc),
+        "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(src)
+        : "memory");
+}
+
 // ------------------------------------------------ 1-D bulk copies (TMA) --
 // shared -> global, tracked by this thread's bulk groups (no mbarrier).
 __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {

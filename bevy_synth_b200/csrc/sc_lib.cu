@@ -125,6 +125,14 @@ static int gather4_mode() {
     return v == 1 || v == 2 ? v : 0;
 }
 
+static bool use_tma_epilogue() {
+    static const bool v = [] {
+        const char* e = std::getenv("SC_TC_TMA_EPI");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 static bool allow_pair() {
     const char* e = std::getenv("SC_TC_PAIR");
     return e && e[0] == '1';
@@ -189,7 +197,7 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     } else if (!stg_env) {
         const int stg64 = tc_stg_cols(tile_n, 64);
         const int s64 = deepest(stg64);
-        if (s64 > S) {
+        if (s64 >= S) {  // ties take 64 columns: the TMA (scatter4 / gather4) epilogue needs them
             stg = stg64;
             S = s64;
         }
@@ -239,9 +247,35 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
             return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled (features) failed with code " + std::to_string((int)ra));
     }
 
+    // Epilogue through TMA row gathers / scatters: 64-column staging, outputs that
+    // are plain rows (no child-row scatter); maps are [rows, cols] bf16, 64-column boxes.
+    CUtensorMap omap, o2map, rmap;
+    memset(&omap, 0, sizeof omap);
+    memset(&o2map, 0, sizeof o2map);
+    memset(&rmap, 0, sizeof rmap);
+    const bool tma_epi = use_tma_epilogue() && plan.stg_cols == 64 && e.d_out_row_map == nullptr &&
+                         n_rows > 0 && n_rows < 0x7fffffff;
+    if (tma_epi) {
+        auto enc_rows = [&](CUtensorMap* m, const void* base) -> CUresult {
+            cuuint64_t d[2] = {(cuuint64_t)cout, (cuuint64_t)n_rows};
+            cuuint64_t sd[1] = {(cuuint64_t)cout * 2};
+            cuuint32_t bx[2] = {64u, 1u};
+            cuuint32_t es[2] = {1u, 1u};
+            return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), d, sd, bx, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        };
+        CUresult r1 = enc_rows(&omap, out);
+        CUresult r2 = e.d_out2 ? enc_rows(&o2map, e.d_out2) : CUDA_SUCCESS;
+        CUresult r3 = (e.d_residual && !e.d_residual_offset) ? enc_rows(&rmap, e.d_residual) : CUDA_SUCCESS;
+        if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS || r3 != CUDA_SUCCESS)
+            return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled (epilogue) failed");
+    }
+
     TcParams p;
     memset(&p, 0, sizeof p);
     p.gather4 = g4 ? g4_mode : 0;
+    p.tma_epi = tma_epi ? 1 : 0;
     p.in = static_cast<const __nv_bfloat16*>(in);
     p.n_in = n_in;
     p.cin = (int)cin;
@@ -294,7 +328,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
         p.dynamic = use_static_schedule() ? 0 : 1;
         const int64_t ctas = p.dynamic ? p.n_tiles : std::min<int64_t>(p.n_tiles, sm_count());
         if (ctas > 0x7fffffff) return fail(SC_ERR_UNSUPPORTED, "too many row tiles for one launch");
-        conv_tc_kernel<false><<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, amap, p);
+        conv_tc_kernel<false><<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
     } else {
         cudaLaunchConfig_t lc;
         memset(&lc, 0, sizeof lc);
@@ -315,7 +349,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
             max_clusters = sm_count() / 2;
         const int64_t pairs = std::min<int64_t>(p.n_tiles, max_clusters);
         lc.gridDim = dim3((unsigned)(2 * pairs));
-        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true>, wmap, amap, p));
+        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true>, wmap, amap, omap, o2map, rmap, p));
     }
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
