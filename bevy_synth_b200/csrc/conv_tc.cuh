@@ -885,14 +885,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         !(p.tma_epi ? load_staged_tma(st, row, &rmap, n0 + g0, p.n_rows, lane, &res_bar[warp], res_ph)
                                     : load_staged_rows(st, row, p.residual, p.cout, n0 + g0, lane, &res_bar[warp], res_ph)))
                         *abort_flag = 1u;
-                    for (int c = g0; c < g0 + stg_cols; c += 32) {
-                        float v[32];
-                        compute_y(c, g0, v);
-                        if (p.silu) {
+                    for (int c = g0; c < g0 + stg_cols;) {
+                        if (c + 64 <= g0 + stg_cols && !p.res_off) {
+                            // 64 columns per TMEM wait
+                            float v[64];
+                            tmem_ld64(lane_addr + c, v);
+                            float (&lo)[32] = *reinterpret_cast<float(*)[32]>(v);
+                            float (&hi)[32] = *reinterpret_cast<float(*)[32]>(v + 32);
+                            if (p.bias) {
+                                add_param32(lo, p.bias + n0 + c, false);
+                                add_param32(hi, p.bias + n0 + c + 32, false);
+                            }
+                            if (dense_res) {
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
+                                for (int q = 0; q < 8; ++q) {
+                                    float r8[8];
+                                    load_bf16x8(st.at(lane, (c - g0) / 8 + q), r8);
+#pragma unroll
+                                    for (int e = 0; e < 8; ++e) v[q * 8 + e] += r8[e];
+                                }
+                            }
+                            if (p.silu) {
+#pragma unroll
+                                for (int e = 0; e < 64; ++e) v[e] = silu_bf16out(v[e]);
+                            }
+                            stage_out(c, g0, lo);
+                            stage_out(c + 32, g0, hi);
+                            c += 64;
+                        } else {
+                            float v[32];
+                            compute_y(c, g0, v);
+                            if (p.silu) {
+#pragma unroll
+                                for (int e = 0; e < 32; ++e) v[e] = silu_bf16out(v[e]);
+                            }
+                            stage_out(c, g0, v);
+                            c += 32;
                         }
-                        stage_out(c, g0, v);
                     }
                     __syncwarp();
                     if (p.tma_epi)
@@ -998,7 +1027,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                         if (p.silu) {
 #pragma unroll
-                            for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
+                            for (int e = 0; e < 32; ++e) v[e] = silu_bf16out(v[e]);
                         }
                         stage_out(c, g0, v);
                     }

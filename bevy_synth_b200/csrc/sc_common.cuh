@@ -73,6 +73,15 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { retu
 // burn_trellis sparse_decoder_wgpu_ops.rs:1713-1720), evaluated with CUDA's
 // fast-math intrinsics __expf and __fdividef (results are stored as bf16).
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// SiLU for bf16 outputs with one special-function op: x*sigmoid(x) = h + h*tanh(h),
+// h = x/2, using the hardware tanh approximation (relative error ~2^-11, below
+// the bf16 rounding of the stored result).
+__device__ __forceinline__ float silu_bf16out(float x) {
+    const float h = 0.5f * x;
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+    return fmaf(h, t, h);
+}
 
 // ------------------------------------------------------------- smem/mbar --
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
