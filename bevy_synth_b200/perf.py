@@ -171,7 +171,31 @@ def run_convnext(dev, t):
                   stack.launches(), {"voxels": int(n)})]
 
 
-WORKLOADS = {"cfg1": run_cfg1, "cfg3": run_cfg3, "cfg4": run_cfg4, "cfg5": run_cfg5, "convnext": run_convnext}
+def run_gather(dev, t):
+    """Random 128-byte row gather bandwidth by copy method (micro/gather_bw.cu), the
+    bound of the gather-limited small-channel layers."""
+    import re
+    import subprocess
+
+    from .build import nvcc
+    here = os.path.dirname(os.path.abspath(__file__))
+    src = os.path.join(here, "micro", "gather_bw.cu")
+    exe = os.path.join(here, "micro", "gather_bw")
+    if not os.path.exists(exe) or os.path.getmtime(exe) < os.path.getmtime(src):
+        subprocess.run([nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
+                        "-I" + os.path.join(_ROOT, "include"), "-o", exe, src, "-lcuda"], check=True)
+    txt = subprocess.run([exe], check=True, capture_output=True, text=True).stdout
+    out = []
+    for line in txt.splitlines():
+        m = re.match(r"(.+?)\s+([\d.]+) TB/s\s+([\d.]+) B/clk", line)
+        if m:
+            out.append({"workload": "gather_bw", "method": m.group(1).strip(), "tb_per_s": float(m.group(2)),
+                        "bytes_per_clk_per_sm_at_1.9ghz": float(m.group(3))})
+    return out
+
+
+WORKLOADS = {"cfg1": run_cfg1, "cfg3": run_cfg3, "cfg4": run_cfg4, "cfg5": run_cfg5, "convnext": run_convnext,
+             "gather": run_gather}
 
 
 def main(argv=None):
