@@ -55,15 +55,14 @@ namespace sc {
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;                      // channels per reduction step
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
-#ifndef SC_TC_PW
-#define SC_TC_PW 4
-#endif
-// Gather producer warps.  One per SM sub-partition: the cp.async issue queue
-// is per sub-partition, and with two warps it, not the tensor pipe, set the
-// stage rate.
-constexpr int TC_PW = SC_TC_PW;
-static_assert(TC_PW == 2 || TC_PW == 4 || TC_PW == 8, "producer warps");
-constexpr int TC_THREADS = (4 + TC_PW + 1) * 32;
+// Gather producer warps (a kernel template parameter, 4 or 8): one or two per SM
+// sub-partition.  A producer warp's per-stage instruction stream (empty wait, row
+// indices, address math, copies, arrive) is latency-bound, so the stage rate of a
+// 3x3x3 conv scales with the warps that interleave on a sub-partition; 8 warps
+// leave 128 registers a thread (13 warps, 4 on one sub-partition), which the 1x1
+// (linear) convs, epilogue-bound, do not trade for.
+constexpr int TC_PW_MAX = 8;
+__host__ __device__ constexpr int tc_threads(int pw) { return (4 + pw + 1) * 32; }
 constexpr int TC_MAX_K = 32;
 constexpr int TC_STG_COLS = 128;               // epilogue staging width (columns)
 constexpr int TC_SCHED = 4;                    // launch-control responses in flight (ring)
@@ -256,11 +255,12 @@ __device__ __forceinline__ void add_param32(float (&v)[32], const float* p, bool
     }
 }
 
-template <bool PAIR>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <bool PAIR, int TC_PW>
+__global__ void __launch_bounds__(tc_threads(TC_PW), 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap omap, const __grid_constant__ CUtensorMap o2map,
                    const __grid_constant__ CUtensorMap rmap, const TcParams p) {
+    static_assert(TC_PW == 4 || TC_PW == 8, "producer warps");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1083,7 +1083,7 @@ inline int tc_stg_cols(int tile_n, int cap = TC_STG_COLS) {
 inline size_t tc_smem_bytes(int stages, int tile_n, int K, bool pair, int stg_cols) {
     const size_t b_bytes = (size_t)(pair ? tile_n / 2 : tile_n) * 128;
     return 1024 + (size_t)stages * (TC_A_BYTES + b_bytes) + 4 * 32 * (stg_cols / 8 + 1) * 16 +
-           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 8 * TC_PW + 8 + 8 + 4 * 8;
+           (size_t)TC_BM * K * 4 + (3 * stages + 4) * 8 + stages * 4 + 32 + 16 + TC_SCHED * (16 + 16) + 8 + 8 * TC_PW_MAX + 8 + 8 + 4 * 8;
 }
 
 }  // namespace sc

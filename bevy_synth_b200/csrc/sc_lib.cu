@@ -102,6 +102,7 @@ static bool force_simt() {
 
 struct TcPlan {
     int tile_n, n_sub, sub_n, stages, grid_y, n_buf, stg_cols;
+    int pw;     // gather producer warps of the kernel instance (4 or 8)
     bool pair;  // 2-SM (cta_group::2) kernel on CTA pairs
     size_t smem;
 };
@@ -181,6 +182,11 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     plan->n_buf = tile_n <= 256 ? 2 : 1;
     plan->grid_y = (int)(cout / tile_n);
     plan->pair = allow_pair() && plan->sub_n >= 32 && c->in_channels % 8 == 0;
+    // 8 gather warps for multi-tap convs (their producer instruction stream sets the stage
+    // rate), 4 for 1x1 convs and the pair kernel (SC_TC_PW=4|8 pins it on the single-CTA kernel)
+    plan->pw = (!plan->pair && K > 1) ? 8 : 4;
+    if (const char* pw_env = std::getenv("SC_TC_PW"))
+        if (!plan->pair && (std::atoi(pw_env) == 4 || std::atoi(pw_env) == 8)) plan->pw = std::atoi(pw_env);
     // Deepest stage ring that fits; a narrower epilogue staging buffer is
     // taken when it buys a stage (SC_TC_STG=64|128 pins the width).
     auto deepest = [&](int stg) {
@@ -314,10 +320,13 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(conv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        attr_err = cudaFuncSetAttribute(conv_tc_kernel<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)kMaxDynSmem);
         if (attr_err == cudaSuccess)
-            attr_err = cudaFuncSetAttribute(conv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            attr_err = cudaFuncSetAttribute(conv_tc_kernel<false, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)kMaxDynSmem);
+        if (attr_err == cudaSuccess)
+            attr_err = cudaFuncSetAttribute(conv_tc_kernel<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)kMaxDynSmem);
     });
     SC_CUDA_TRY(attr_err);
@@ -328,7 +337,10 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
         p.dynamic = use_static_schedule() ? 0 : 1;
         const int64_t ctas = p.dynamic ? p.n_tiles : std::min<int64_t>(p.n_tiles, sm_count());
         if (ctas > 0x7fffffff) return fail(SC_ERR_UNSUPPORTED, "too many row tiles for one launch");
-        conv_tc_kernel<false><<<(unsigned)ctas, TC_THREADS, plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
+        if (plan.pw == 8)
+            conv_tc_kernel<false, 8><<<(unsigned)ctas, tc_threads(8), plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
+        else
+            conv_tc_kernel<false, 4><<<(unsigned)ctas, tc_threads(4), plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
     } else {
         cudaLaunchConfig_t lc;
         memset(&lc, 0, sizeof lc);
@@ -337,19 +349,19 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
-        lc.blockDim = dim3(TC_THREADS);
+        lc.blockDim = dim3(tc_threads(4));
         lc.dynamicSmemBytes = plan.smem;
         lc.stream = st;
         lc.attrs = attr;
         lc.numAttrs = 1;
         lc.gridDim = dim3((unsigned)(2 * sm_count()));
         int max_clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&max_clusters, conv_tc_kernel<true>, &lc) != cudaSuccess ||
+        if (cudaOccupancyMaxActiveClusters(&max_clusters, conv_tc_kernel<true, 4>, &lc) != cudaSuccess ||
             max_clusters <= 0)
             max_clusters = sm_count() / 2;
         const int64_t pairs = std::min<int64_t>(p.n_tiles, max_clusters);
         lc.gridDim = dim3((unsigned)(2 * pairs));
-        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true>, wmap, amap, omap, o2map, rmap, p));
+        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true, 4>, wmap, amap, omap, o2map, rmap, p));
     }
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
