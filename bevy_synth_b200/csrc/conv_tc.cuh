@@ -255,7 +255,14 @@ __device__ __forceinline__ void add_param32(float (&v)[32], const float* p, bool
     }
 }
 
-template <bool PAIR, int TC_PW>
+// MODE: the producer features a launch compiles in.  TC_LEAN: a pre-ordered (or unordered)
+// map, cp.async gathers only; TC_DRY: + dry stages for scatter convs (C2S conv1);
+// TC_FULL: + TMA gather4 modes and row orders without a pre-ordered map.  The lean
+// instances run the same stages with a shorter producer loop (gather-bound layers ~15%
+// faster than the full instance).
+constexpr int TC_LEAN = 0, TC_DRY = 1, TC_FULL = 2;
+
+template <bool PAIR, int TC_PW, int MODE>
 __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap omap, const __grid_constant__ CUtensorMap o2map,
@@ -381,14 +388,18 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
         int64_t tile = first_tile;
         int64_t requested = 0;  // launch-control requests issued (producer warp 0)
         int64_t issued = 0;     // stages this warp has issued
+        // Stages of every kind, counted alike by all producer warps: stage i's B tile (and the
+        // flags the MMA thread reads) is issued by warp i % TC_PW, so no one warp carries the
+        // extra per-stage work and sets the pace of the stage ring.
+        uint32_t stage_no = 0;
         // Contiguous map rows (no row order, or a pre-ordered map) on one CTA:
         // each producer warp reads only its own rows' map block, one tile
         // ahead, into registers (16-byte loads, all in flight at once), and
         // the two warps OR their tap masks through mask_bar.
-        const bool fast_map = p.row_order == nullptr || p.nbr_ordered != nullptr;
+        const bool fast_map = MODE != TC_FULL || p.row_order == nullptr || p.nbr_ordered != nullptr;
         // gather4 == 2 (single CTA): the upper half of the producer warps gather by TMA, the lower
         // half by cp.async, so both copy engines carry A rows
-        const bool G4 = p.gather4 == 1 || (!PAIR && p.gather4 == 2 && pw >= TC_PW / 2);
+        const bool G4 = MODE == TC_FULL && (p.gather4 == 1 || (!PAIR && p.gather4 == 2 && pw >= TC_PW / 2));
         const int32_t* map_rows = p.nbr_ordered ? p.nbr_ordered : p.nbr;
         constexpr int QV = (ROWS * TC_MAX_K / 4 + 31) / 32;  // int4 per lane for ROWS rows of <= 32 taps
         const int my_vec = ROWS * K / 4;                       // int4 of my rows' block (K * 64 / 4)
@@ -575,7 +586,7 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
             // this block writes nothing: run it as one "dry" stage (no copies; the MMAs read stale
             // shared memory into an accumulator whose rows are all discarded).
             bool dry = false;
-            if (!PAIR && p.gather4 == 0 && p.row_map != nullptr && p.map_cols > 1) {
+            if (MODE != TC_LEAN && !PAIR && p.gather4 == 0 && p.row_map != nullptr && p.map_cols > 1) {
                 const int wb = p.cout / p.map_cols;
                 const int blk = n0 / wb;
                 bool kept = false;
@@ -592,28 +603,39 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
             if (dry) mask = mask & (~mask + 1u);  // the lowest valid tap only
             const int n_steps = __popc(mask) * chunks;
             int step = 0;
-            for (uint32_t m = mask; m && ok; m &= m - 1) {
-                const int k = __ffs(m) - 1;
-                int32_t src[GROUPS];
+            // Source rows of tap kk for this lane's copies.  They are read one tap ahead, so the
+            // shared-memory loads overlap the current tap's stages instead of heading them.
+            auto load_rows = [&](int kk, int32_t (&d)[GROUPS]) {
                 if (G4) {
                     // lanes below ROWS/4: the four rows 4*lane .. 4*lane+3 of my rows (absent rows read as zeros)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const int32_t v = lane < ROWS / 4 ? my_nbr[(4 * lane + e) * K + k] : -1;
-                        src[e] = v >= 0 ? v : (int32_t)p.n_in;
+                        const int32_t v = lane < ROWS / 4 ? my_nbr[(4 * lane + e) * K + kk] : -1;
+                        d[e] = v >= 0 ? v : (int32_t)p.n_in;
                     }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < GROUPS; ++i) src[i] = my_nbr[(i * 4 + sub) * K + k];
+                    for (int i = 0; i < GROUPS; ++i) d[i] = my_nbr[(i * 4 + sub) * K + kk];
                 }
+            };
+            int32_t next_rows[GROUPS];
+            load_rows(__ffs(mask) - 1, next_rows);
+            for (uint32_t m = mask; m && ok; m &= m - 1) {
+                const int k = __ffs(m) - 1;
+                int32_t src[GROUPS];
+#pragma unroll
+                for (int i = 0; i < GROUPS; ++i) src[i] = next_rows[i];
+                const uint32_t m_next = m & (m - 1);
+                if (m_next) load_rows(__ffs(m_next) - 1, next_rows);
                 for (int ch = 0; ch < chunks; ++ch, ++step) {
                     if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u))) {
                         ok = false;
                         break;
                     }
+                    const bool b_lane = lane == 0 && (int)(stage_no++ & (uint32_t)(TC_PW - 1)) == pw;
                     if (dry) {
                         // every arrival the stage expects, no copies
-                        if (pw == 0 && lane == 0) {
+                        if (b_lane) {
                             if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
                             stage_flags[s] = 2u;
                             mbar_arrive(&full[s]);
@@ -657,7 +679,7 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
                         }
                         continue;
                     }
-                    if (pw == 0 && lane == 0) {
+                    if (b_lane) {
                         // published to the MMA thread by this stage's full-barrier arrive below
                         if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
                         stage_flags[s] = step == n_steps - 1 ? 2u : 0u;

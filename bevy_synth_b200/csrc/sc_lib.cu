@@ -320,14 +320,12 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once, [] {
-        attr_err = cudaFuncSetAttribute(conv_tc_kernel<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)kMaxDynSmem);
-        if (attr_err == cudaSuccess)
-            attr_err = cudaFuncSetAttribute(conv_tc_kernel<false, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)kMaxDynSmem);
-        if (attr_err == cudaSuccess)
-            attr_err = cudaFuncSetAttribute(conv_tc_kernel<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)kMaxDynSmem);
+        const void* fns[] = {(const void*)conv_tc_kernel<false, 4, TC_LEAN>, (const void*)conv_tc_kernel<false, 4, TC_FULL>,
+                             (const void*)conv_tc_kernel<false, 8, TC_LEAN>, (const void*)conv_tc_kernel<false, 8, TC_DRY>,
+                             (const void*)conv_tc_kernel<true, 4, TC_FULL>};
+        for (const void* f : fns)
+            if (attr_err == cudaSuccess)
+                attr_err = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem);
     });
     SC_CUDA_TRY(attr_err);
     if (!plan.pair) {
@@ -337,10 +335,18 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
         p.dynamic = use_static_schedule() ? 0 : 1;
         const int64_t ctas = p.dynamic ? p.n_tiles : std::min<int64_t>(p.n_tiles, sm_count());
         if (ctas > 0x7fffffff) return fail(SC_ERR_UNSUPPORTED, "too many row tiles for one launch");
-        if (plan.pw == 8)
-            conv_tc_kernel<false, 8><<<(unsigned)ctas, tc_threads(8), plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
+        // the leanest instance that has every producer feature this launch uses
+        const bool full = p.gather4 != 0 || (p.row_order != nullptr && p.nbr_ordered == nullptr);
+        const bool dry = p.row_map != nullptr && p.map_cols > 1;
+        const dim3 g((unsigned)ctas);
+        if (plan.pw == 8 && !full && !dry)
+            conv_tc_kernel<false, 8, TC_LEAN><<<g, tc_threads(8), plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
+        else if (plan.pw == 8 && !full)
+            conv_tc_kernel<false, 8, TC_DRY><<<g, tc_threads(8), plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
+        else if (!full && !dry)
+            conv_tc_kernel<false, 4, TC_LEAN><<<g, tc_threads(4), plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
         else
-            conv_tc_kernel<false, 4><<<(unsigned)ctas, tc_threads(4), plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
+            conv_tc_kernel<false, 4, TC_FULL><<<g, tc_threads(4), plan.smem, st>>>(wmap, amap, omap, o2map, rmap, p);
     } else {
         cudaLaunchConfig_t lc;
         memset(&lc, 0, sizeof lc);
@@ -356,12 +362,12 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
         lc.numAttrs = 1;
         lc.gridDim = dim3((unsigned)(2 * sm_count()));
         int max_clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&max_clusters, conv_tc_kernel<true, 4>, &lc) != cudaSuccess ||
+        if (cudaOccupancyMaxActiveClusters(&max_clusters, conv_tc_kernel<true, 4, TC_FULL>, &lc) != cudaSuccess ||
             max_clusters <= 0)
             max_clusters = sm_count() / 2;
         const int64_t pairs = std::min<int64_t>(p.n_tiles, max_clusters);
         lc.gridDim = dim3((unsigned)(2 * pairs));
-        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true, 4>, wmap, amap, omap, o2map, rmap, p));
+        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true, 4, TC_FULL>, wmap, amap, omap, o2map, rmap, p));
     }
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
