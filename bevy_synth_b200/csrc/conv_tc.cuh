@@ -632,7 +632,10 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
                         ok = false;
                         break;
                     }
-                    const bool b_lane = lane == 0 && (int)(stage_no++ & (uint32_t)(TC_PW - 1)) == pw;
+                    // (the full instance keeps warp 0: with gather4 == 2 only the lower warps take this path)
+                    const bool b_lane = lane == 0 && (MODE == TC_FULL ? pw == 0
+                                                                      : (int)(stage_no & (uint32_t)(TC_PW - 1)) == pw);
+                    ++stage_no;
                     if (dry) {
                         // every arrival the stage expects, no copies
                         if (b_lane) {
