@@ -186,7 +186,7 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     // rate), 4 for 1x1 convs and the pair kernel (SC_TC_PW=4|8 pins it on the single-CTA kernel)
     plan->pw = (!plan->pair && K > 1) ? 8 : 4;
     if (const char* pw_env = std::getenv("SC_TC_PW"))
-        if (!plan->pair && (std::atoi(pw_env) == 4 || std::atoi(pw_env) == 8)) plan->pw = std::atoi(pw_env);
+        if (std::atoi(pw_env) == 4 || std::atoi(pw_env) == 8) plan->pw = std::atoi(pw_env);
     // Deepest stage ring that fits; a narrower epilogue staging buffer is
     // taken when it buys a stage (SC_TC_STG=64|128 pins the width).
     auto deepest = [&](int stg) {
@@ -322,7 +322,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     std::call_once(attr_once, [] {
         const void* fns[] = {(const void*)conv_tc_kernel<false, 4, TC_LEAN>, (const void*)conv_tc_kernel<false, 4, TC_FULL>,
                              (const void*)conv_tc_kernel<false, 8, TC_LEAN>, (const void*)conv_tc_kernel<false, 8, TC_DRY>,
-                             (const void*)conv_tc_kernel<true, 4, TC_FULL>};
+                             (const void*)conv_tc_kernel<true, 4, TC_FULL>, (const void*)conv_tc_kernel<true, 8, TC_LEAN>};
         for (const void* f : fns)
             if (attr_err == cudaSuccess)
                 attr_err = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem);
@@ -355,19 +355,24 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
-        lc.blockDim = dim3(tc_threads(4));
+        // SC_TC_PW=8 (tuning): the 8-warp lean pair instance, when the launch needs no full-instance feature
+        const bool pair8 = plan.pw == 8 && p.gather4 == 0 && !(p.row_order != nullptr && p.nbr_ordered == nullptr);
+        const void* fn = pair8 ? (const void*)conv_tc_kernel<true, 8, TC_LEAN> : (const void*)conv_tc_kernel<true, 4, TC_FULL>;
+        lc.blockDim = dim3(tc_threads(pair8 ? 8 : 4));
         lc.dynamicSmemBytes = plan.smem;
         lc.stream = st;
         lc.attrs = attr;
         lc.numAttrs = 1;
         lc.gridDim = dim3((unsigned)(2 * sm_count()));
         int max_clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&max_clusters, conv_tc_kernel<true, 4, TC_FULL>, &lc) != cudaSuccess ||
-            max_clusters <= 0)
+        if (cudaOccupancyMaxActiveClusters(&max_clusters, fn, &lc) != cudaSuccess || max_clusters <= 0)
             max_clusters = sm_count() / 2;
         const int64_t pairs = std::min<int64_t>(p.n_tiles, max_clusters);
         lc.gridDim = dim3((unsigned)(2 * pairs));
-        SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true, 4, TC_FULL>, wmap, amap, omap, o2map, rmap, p));
+        if (pair8)
+            SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true, 8, TC_LEAN>, wmap, amap, omap, o2map, rmap, p));
+        else
+            SC_CUDA_TRY(cudaLaunchKernelEx(&lc, conv_tc_kernel<true, 4, TC_FULL>, wmap, amap, omap, o2map, rmap, p));
     }
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;

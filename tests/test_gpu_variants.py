@@ -44,6 +44,7 @@ VARIANTS = {
     "tma_gather4": {"SC_TC_GATHER4": "1"},
     "half_tma_gather4": {"SC_TC_GATHER4": "2"},
     "cta_pair": {"SC_TC_PAIR": "1"},
+    "cta_pair_eight_gather_warps": {"SC_TC_PAIR": "1", "SC_TC_PW": "8"},
     "static_schedule": {"SC_TC_STATIC": "1"},
 }
 
