@@ -134,9 +134,11 @@ static bool use_tma_epilogue() {
     return v;
 }
 
-static bool allow_pair() {
+// SC_TC_PAIR=1 takes the pair kernel wherever it applies, SC_TC_PAIR=0 nowhere; unset, it is taken for
+// narrow multi-tap convs (Cin and Cout <= 64), the one shape class where it measured faster.
+static int pair_mode() {
     const char* e = std::getenv("SC_TC_PAIR");
-    return e && e[0] == '1';
+    return !e ? -1 : (e[0] == '1' ? 1 : 0);
 }
 
 static constexpr size_t kMaxDynSmem = 232448;  // 227 KB opt-in per block on sm_100
@@ -181,10 +183,12 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     if (plan->sub_n % 16 != 0) return false;
     plan->n_buf = tile_n <= 256 ? 2 : 1;
     plan->grid_y = (int)(cout / tile_n);
-    plan->pair = allow_pair() && plan->sub_n >= 32 && c->in_channels % 8 == 0;
+    const int pm = pair_mode();
+    const bool narrow = K > 1 && cin <= 64 && cout <= 64 && !e.d_out_row_map && gather4_mode() == 0;
+    plan->pair = (pm == 1 || (pm < 0 && narrow)) && plan->sub_n >= 32 && c->in_channels % 8 == 0;
     // 8 gather warps for multi-tap convs (their producer instruction stream sets the stage
     // rate), 4 for 1x1 convs and the pair kernel (SC_TC_PW=4|8 pins it on the single-CTA kernel)
-    plan->pw = (!plan->pair && K > 1) ? 8 : 4;
+    plan->pw = (K > 1 && (!plan->pair || (pm < 0 && narrow))) ? 8 : 4;
     if (const char* pw_env = std::getenv("SC_TC_PW"))
         if (std::atoi(pw_env) == 4 || std::atoi(pw_env) == 8) plan->pw = std::atoi(pw_env);
     // Deepest stage ring that fits; a narrower epilogue staging buffer is

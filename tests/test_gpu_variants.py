@@ -4,7 +4,7 @@ The launcher reads its tuning switches (SC_TC_*) once per process, so each
 variant runs in a child process on the same seeded inputs and writes its
 outputs to a file; the parent compares them with the default variant's.  The
 variants change scheduling and copy engines only (4 or 8 gather warps, TMA
-row gathers, CTA pairs, a persistent static schedule), never the order of the
+row gathers, CTA pairs on or off, a persistent static schedule), never the order of the
 fp32 accumulation, so the comparison bound is tight.
 """
 import os
@@ -44,6 +44,7 @@ VARIANTS = {
     "tma_gather4": {"SC_TC_GATHER4": "1"},
     "half_tma_gather4": {"SC_TC_GATHER4": "2"},
     "cta_pair": {"SC_TC_PAIR": "1"},
+    "no_cta_pair": {"SC_TC_PAIR": "0"},
     "cta_pair_eight_gather_warps": {"SC_TC_PAIR": "1", "SC_TC_PW": "8"},
     "static_schedule": {"SC_TC_STATIC": "1"},
 }
