@@ -154,6 +154,159 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(
     }
 }
 
+// fp32 gather-GEMM with 8x8 outputs per thread (the fp32 path's main kernel).
+// A 64-row x 64-column output tile per 64-thread CTA; reduction steps of 16
+// input channels of one tap, staged in shared memory (A transposed to
+// [channel][row], B to [channel][column]) and double-buffered: the next step's
+// 16-byte global loads are in registers while the current step's 16 x 64 FMAs
+// per thread run.  The tile's neighbor rows are read once into shared memory
+// and taps with no valid row in the tile are skipped.  Small CTAs keep many
+// tiles per SM, so a 21k-row layer (~340 tiles) still spreads over all SMs.
+// Taken for fp32, groups == 1, Cin % 16 == 0, Cout % 64 == 0, K <= 32, with
+// 16-byte aligned features and weights; other shapes use conv_simt_kernel.
+constexpr int F32_BM = 64, F32_BN = 64, F32_BK = 16, F32_THREADS = 64, F32_MAX_K = 32;
+
+__global__ void __launch_bounds__(F32_THREADS) conv_f32_tiled_kernel(
+    const float* __restrict__ in, int64_t n_in, int cin, const int32_t* __restrict__ nbr, int64_t n_rows, int K,
+    const float* __restrict__ w, const float* __restrict__ bias, int cout, EpiParams epi) {
+    __shared__ __align__(16) float As[2][F32_BK][F32_BM];
+    __shared__ __align__(16) float Bs[2][F32_BK][F32_BN];
+    __shared__ int32_t nb_s[F32_MAX_K][F32_BM];
+    __shared__ uint32_t tap_mask;
+
+    const int tid = threadIdx.x;
+    const int ty = tid >> 3, tx = tid & 7;  // compute: rows ty*8.., columns tx*8..
+    const int64_t row0 = (int64_t)blockIdx.x * F32_BM;
+    const int col0 = blockIdx.y * F32_BN;
+
+    if (tid == 0) tap_mask = 0u;
+    __syncthreads();
+    {
+        // this thread's tile row: its neighbor rows (checked) and valid-tap bits
+        int64_t r = row0 + tid;
+        if (r < n_rows && epi.row_order) {
+            r = epi.row_order[r];
+            if (r < 0 || r >= n_rows) {
+                raise_fault(FAULT_BAD_NEIGHBOR);
+                r = n_rows;
+            }
+        }
+        uint32_t m = 0;
+        for (int k = 0; k < K; ++k) {
+            int32_t v = -1;
+            if (r < n_rows) {
+                v = __ldg(nbr + r * K + k);
+                if (v < -1 || v >= n_in) {
+                    raise_fault(FAULT_BAD_NEIGHBOR);
+                    v = -1;
+                }
+            }
+            nb_s[k][tid] = v;
+            if (v >= 0) m |= 1u << k;
+        }
+        m = __reduce_or_sync(0xffffffffu, m);
+        if ((tid & 31) == 0) atomicOr(&tap_mask, m);
+    }
+    __syncthreads();
+    const uint32_t mask = tap_mask;
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+    // global -> registers for step (k, c0): A row `tid` (16 channels), B column `tid` (16 channels)
+    float4 ra[4], rb[4];
+    auto gload = [&](int k, int c0) {
+        const int32_t src = nb_s[k][tid];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            ra[q] = src >= 0 ? __ldg(reinterpret_cast<const float4*>(in + (int64_t)src * cin + c0) + q)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float* wp = w + ((int64_t)(col0 + tid) * K + k) * cin + c0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) rb[q] = __ldg(reinterpret_cast<const float4*>(wp) + q);
+    };
+    auto sstore = [&](int b) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            As[b][4 * q + 0][tid] = ra[q].x;
+            As[b][4 * q + 1][tid] = ra[q].y;
+            As[b][4 * q + 2][tid] = ra[q].z;
+            As[b][4 * q + 3][tid] = ra[q].w;
+            Bs[b][4 * q + 0][tid] = rb[q].x;
+            Bs[b][4 * q + 1][tid] = rb[q].y;
+            Bs[b][4 * q + 2][tid] = rb[q].z;
+            Bs[b][4 * q + 3][tid] = rb[q].w;
+        }
+    };
+
+    if (mask) {
+        uint32_t m = mask;
+        int k = __ffs(m) - 1, c0 = 0;
+        gload(k, c0);
+        sstore(0);
+        __syncthreads();
+        for (int b = 0;; b ^= 1) {
+            // the next step: next channel slice of this tap, else the next valid tap
+            int nk = k, nc = c0 + F32_BK;
+            if (nc >= cin) {
+                m &= m - 1;
+                nk = m ? __ffs(m) - 1 : -1;
+                nc = 0;
+            }
+            if (nk >= 0) gload(nk, nc);
+#pragma unroll
+            for (int kk = 0; kk < F32_BK; ++kk) {
+                const float4 a0 = *reinterpret_cast<const float4*>(&As[b][kk][ty * 8]);
+                const float4 a1 = *reinterpret_cast<const float4*>(&As[b][kk][ty * 8 + 4]);
+                const float4 b0 = *reinterpret_cast<const float4*>(&Bs[b][kk][tx * 8]);
+                const float4 b1 = *reinterpret_cast<const float4*>(&Bs[b][kk][tx * 8 + 4]);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+            }
+            if (nk < 0) break;
+            sstore(b ^ 1);
+            __syncthreads();
+            k = nk;
+            c0 = nc;
+        }
+    }
+
+    // epilogue: bias, residual, scatter (as conv_simt_kernel)
+    const float* res = reinterpret_cast<const float*>(epi.residual);
+    float* out = reinterpret_cast<float*>(epi.out);
+    const int wb = epi.row_map ? cout / epi.map_cols : cout;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        int64_t r = row0 + ty * 8 + i;
+        if (r >= n_rows) continue;
+        if (epi.row_order) {
+            r = epi.row_order[r];
+            if (r < 0 || r >= n_rows) continue;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int o = col0 + tx * 8 + j;
+            float v = acc[i][j] + (bias ? bias[o] : 0.f);
+            if (res) v += load_residual<float>(res, epi.res_off, epi.res_rep, r, o, cout);
+            int64_t orow = r;
+            int ocol = o;
+            if (epi.row_map) {
+                orow = epi.row_map[r * epi.map_cols + o / wb];
+                ocol = o % wb;
+                if (orow < 0) continue;
+            }
+            out[orow * wb + ocol] = v;
+        }
+    }
+}
+
 // Row-wise LayerNorm (+affine) and/or SiLU, one warp per entry.  Entry e is
 // the `width` values at element offset row*ld with row = map[e] (or e when
 // map is null; skipped when negative).  Two-pass statistics as the reference

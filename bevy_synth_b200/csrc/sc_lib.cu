@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 #include <string>
 
 #include "conv_simt.cuh"
@@ -397,10 +398,26 @@ static int launch_simt(const sc_conv_config* c, const void* in, int64_t n_in, co
     ep.row_map = e.d_out_row_map;
     ep.map_cols = e.d_out_row_map ? e.out_row_map_cols : 1;
     ep.row_order = e.d_row_order;
-    dim3 grid(grid1d(n_rows, SIMT_BM), (unsigned)(bpg * c->groups));
-    conv_simt_kernel<T><<<grid, 256, 0, st>>>(
-        static_cast<const T*>(in), n_in, (int)c->in_channels, (int)c->in_channels_per_group, nbr,
-        n_rows, (int)K, static_cast<const T*>(w), bias, (int)c->out_channels, cout_g, bpg, ep);
+    bool tiled = false;
+    if constexpr (std::is_same<T, float>::value) {
+        // the 8x8-per-thread fp32 kernel for the common shapes (see conv_f32_tiled_kernel)
+        tiled = c->groups == 1 && c->in_channels % F32_BK == 0 && c->out_channels % F32_BN == 0 &&
+                K <= F32_MAX_K && reinterpret_cast<uintptr_t>(in) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(w) % 16 == 0;
+        if (tiled) {
+            dim3 g(grid1d(n_rows, F32_BM), (unsigned)(c->out_channels / F32_BN));
+            conv_f32_tiled_kernel<<<g, F32_THREADS, 0, st>>>(static_cast<const float*>(in), n_in,
+                                                             (int)c->in_channels, nbr, n_rows, (int)K,
+                                                             static_cast<const float*>(w), bias,
+                                                             (int)c->out_channels, ep);
+        }
+    }
+    if (!tiled) {
+        dim3 grid(grid1d(n_rows, SIMT_BM), (unsigned)(bpg * c->groups));
+        conv_simt_kernel<T><<<grid, 256, 0, st>>>(
+            static_cast<const T*>(in), n_in, (int)c->in_channels, (int)c->in_channels_per_group, nbr,
+            n_rows, (int)K, static_cast<const T*>(w), bias, (int)c->out_channels, cout_g, bpg, ep);
+    }
     SC_CUDA_TRY(cudaGetLastError());
     if (e.layer_norm || e.silu) {
         // post(y) as a second row pass over the stored y

@@ -82,6 +82,50 @@ def test_config1_fp32_full(cuda_device):
     assert_no_fault()
 
 
+@pytest.mark.parametrize("cin,cout,scheduled", [(64, 128, True), (32, 64, False), (128, 64, True)])
+def test_fp32_tiled_kernel_epilogues(cuda_device, cin, cout, scheduled):
+    """The fp32 8x8-per-thread kernel (Cin % 16 == 0, Cout % 64 == 0): bias + residual,
+    a scheduled row order, the LayerNorm/SiLU pass, and a row count that is not a
+    multiple of its 64-row tile."""
+    coords = shell(grid=30, r=10.0, seed=cin)[:-5]
+    n = coords.shape[0]
+    assert n % 64 != 0
+    rng = np.random.default_rng(cin + cout)
+    x = rng.standard_normal((n, cin)).astype(np.float32)
+    w = (rng.standard_normal((cout, 3, 3, 3, cin)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    res = rng.standard_normal((n, cout)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(cout)).astype(np.float32)
+    be = (0.1 * rng.standard_normal(cout)).astype(np.float32)
+    cfg = F.SparseSubmConvConfig.subm3(cin, cout)
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords.astype(np.int32)))
+    sched = F.neighbor_schedule(cfg, nbr) if scheduled else None
+    out2 = torch.empty((n, cout), dtype=torch.float32, device="cuda:0")
+    epi = F.Epilogue(residual=to_dev(res), layer_norm=True, ln_eps=1e-5, ln_gamma=to_dev(g), ln_beta=to_dev(be),
+                     silu=True, out2=out2, schedule=sched)
+    out, _ = conv_gpu(cfg, coords, x, w, b, torch.float32, epi, nbr=nbr)
+    y = oracle.subm_conv_flex(ocfg(cfg), w, b, x, nbr.cpu().numpy(), threads=8) + res
+    assert rel_l2(out, y) <= 1e-4
+    assert np.abs(out - y).max() <= 1e-4 * max(1.0, float(np.abs(y).max()))
+    exp2 = oracle.silu(oracle.layer_norm(y, g, be, 1e-5))
+    assert rel_l2(out2.cpu().numpy(), exp2) <= 1e-4
+    assert_no_fault()
+
+
+def test_fp32_fallback_kernel_odd_channels(cuda_device):
+    """Cin = 24 (not a multiple of 16) and Cout = 40: the generic CUDA-core kernel."""
+    coords = shell(grid=24, r=8.0)
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((coords.shape[0], 24)).astype(np.float32)
+    w = (rng.standard_normal((40, 3, 3, 3, 24)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(40).astype(np.float32)
+    cfg = F.SparseSubmConvConfig.subm3(24, 40)
+    out, nbr = conv_gpu(cfg, coords, x, w, b)
+    exp = oracle.subm_conv_flex(ocfg(cfg), w, b, x, nbr.cpu().numpy(), threads=8)
+    assert rel_l2(out, exp) <= 1e-4
+    assert_no_fault()
+
+
 def bf16_ref(cfg, x, w, b, nbr):
     return oracle.subm_conv_flex(ocfg(cfg), oracle.bf16_round(w), b, oracle.bf16_round(x), nbr, threads=8)
 
