@@ -155,35 +155,50 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(
 }
 
 // fp32 gather-GEMM with 8x8 outputs per thread (the fp32 path's main kernel).
-// A 64-row x 64-column output tile per 64-thread CTA; reduction steps of 16
-// input channels of one tap, staged in shared memory (A transposed to
-// [channel][row], B to [channel][column]) and double-buffered: the next step's
-// 16-byte global loads are in registers while the current step's 16 x 64 FMAs
-// per thread run.  The tile's neighbor rows are read once into shared memory
-// and taps with no valid row in the tile are skipped.  Small CTAs keep many
-// tiles per SM, so a 21k-row layer (~340 tiles) still spreads over all SMs.
+// A 64-row x 64-column output tile per 128-thread CTA: two groups of two warps
+// split the reduction steps (16 input channels of one tap each) between them,
+// each group computing all 64 x 64 outputs in its own registers (8 x 8 per
+// thread) from its own double-buffered shared-memory stages (A transposed to
+// [channel][row], B to [channel][column]); the next step's 16-byte global
+// loads are in registers while the current step's FMAs run, and the next
+// channel's fragments while the current channel's.  Group 1 hands its partial
+// sums to group 0 through shared memory at the end.  The tile's neighbor rows
+// are read once into shared memory and taps with no valid row are skipped.
+// The split doubles the warps per SM of a small layer (a 21k-row layer has only
+// ~340 tiles), which the FMA pipe needs to hide its operand latencies.
 // Taken for fp32, groups == 1, Cin % 16 == 0, Cout % 64 == 0, K <= 32, with
 // 16-byte aligned features and weights; other shapes use conv_simt_kernel.
-constexpr int F32_BM = 64, F32_BN = 64, F32_BK = 16, F32_THREADS = 64, F32_MAX_K = 32;
+constexpr int F32_BM = 64, F32_BN = 64, F32_BK = 16, F32_THREADS = 128, F32_MAX_K = 32;
+
+__device__ __forceinline__ void f32_group_sync(int group) {  // named barrier 1 or 2, 64 threads
+    if (group == 0)
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+    else
+        asm volatile("bar.sync 2, 64;" ::: "memory");
+}
 
 __global__ void __launch_bounds__(F32_THREADS) conv_f32_tiled_kernel(
     const float* __restrict__ in, int64_t n_in, int cin, const int32_t* __restrict__ nbr, int64_t n_rows, int K,
     const float* __restrict__ w, const float* __restrict__ bias, int cout, EpiParams epi) {
-    __shared__ __align__(16) float As[2][F32_BK][F32_BM];
-    __shared__ __align__(16) float Bs[2][F32_BK][F32_BN];
+    // [group][buffer][A | B][channel][row | column]; group 1's half doubles as the partial-sum tile
+    __shared__ __align__(16) float stage[2][2][2][F32_BK][F32_BM];
     __shared__ int32_t nb_s[F32_MAX_K][F32_BM];
+    __shared__ int32_t taps_s[F32_MAX_K];
     __shared__ uint32_t tap_mask;
 
     const int tid = threadIdx.x;
-    const int ty = tid >> 3, tx = tid & 7;  // compute: rows ty*8.., columns tx*8..
+    const int grp = tid >> 6, lt = tid & 63;
+    // compute: rows ty*4+i and 32+ty*4+i, columns tx*4+j and 32+tx*4+j (i, j < 4): each
+    // 16-byte shared-memory read of a warp is then one contiguous 128-byte span
+    const int ty = lt >> 3, tx = lt & 7;
     const int64_t row0 = (int64_t)blockIdx.x * F32_BM;
     const int col0 = blockIdx.y * F32_BN;
 
     if (tid == 0) tap_mask = 0u;
     __syncthreads();
-    {
+    if (grp == 0) {
         // this thread's tile row: its neighbor rows (checked) and valid-tap bits
-        int64_t r = row0 + tid;
+        int64_t r = row0 + lt;
         if (r < n_rows && epi.row_order) {
             r = epi.row_order[r];
             if (r < 0 || r >= n_rows) {
@@ -201,14 +216,21 @@ __global__ void __launch_bounds__(F32_THREADS) conv_f32_tiled_kernel(
                     v = -1;
                 }
             }
-            nb_s[k][tid] = v;
+            nb_s[k][lt] = v;
             if (v >= 0) m |= 1u << k;
         }
         m = __reduce_or_sync(0xffffffffu, m);
-        if ((tid & 31) == 0) atomicOr(&tap_mask, m);
+        if ((lt & 31) == 0) atomicOr(&tap_mask, m);
     }
     __syncthreads();
     const uint32_t mask = tap_mask;
+    if (tid == 0) {
+        int t = 0;
+        for (uint32_t m = mask; m; m &= m - 1) taps_s[t++] = __ffs(m) - 1;
+    }
+    __syncthreads();
+    const int cpt = cin / F32_BK;              // steps per tap
+    const int n_steps = __popc(mask) * cpt;
 
     float acc[8][8];
 #pragma unroll
@@ -216,66 +238,99 @@ __global__ void __launch_bounds__(F32_THREADS) conv_f32_tiled_kernel(
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
-    // global -> registers for step (k, c0): A row `tid` (16 channels), B column `tid` (16 channels)
+    // global -> registers for step st: A row `lt` (16 channels), B column `lt` (16 channels)
     float4 ra[4], rb[4];
-    auto gload = [&](int k, int c0) {
-        const int32_t src = nb_s[k][tid];
+    auto gload = [&](int st) {
+        const int k = taps_s[st / cpt], c0 = (st % cpt) * F32_BK;
+        const int32_t src = nb_s[k][lt];
 #pragma unroll
         for (int q = 0; q < 4; ++q)
             ra[q] = src >= 0 ? __ldg(reinterpret_cast<const float4*>(in + (int64_t)src * cin + c0) + q)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float* wp = w + ((int64_t)(col0 + tid) * K + k) * cin + c0;
+        const float* wp = w + ((int64_t)(col0 + lt) * K + k) * cin + c0;
 #pragma unroll
         for (int q = 0; q < 4; ++q) rb[q] = __ldg(reinterpret_cast<const float4*>(wp) + q);
     };
     auto sstore = [&](int b) {
+        float(*A)[F32_BM] = stage[grp][b][0];
+        float(*B)[F32_BN] = stage[grp][b][1];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            As[b][4 * q + 0][tid] = ra[q].x;
-            As[b][4 * q + 1][tid] = ra[q].y;
-            As[b][4 * q + 2][tid] = ra[q].z;
-            As[b][4 * q + 3][tid] = ra[q].w;
-            Bs[b][4 * q + 0][tid] = rb[q].x;
-            Bs[b][4 * q + 1][tid] = rb[q].y;
-            Bs[b][4 * q + 2][tid] = rb[q].z;
-            Bs[b][4 * q + 3][tid] = rb[q].w;
+            A[4 * q + 0][lt] = ra[q].x;
+            A[4 * q + 1][lt] = ra[q].y;
+            A[4 * q + 2][lt] = ra[q].z;
+            A[4 * q + 3][lt] = ra[q].w;
+            B[4 * q + 0][lt] = rb[q].x;
+            B[4 * q + 1][lt] = rb[q].y;
+            B[4 * q + 2][lt] = rb[q].z;
+            B[4 * q + 3][lt] = rb[q].w;
         }
     };
 
-    if (mask) {
-        uint32_t m = mask;
-        int k = __ffs(m) - 1, c0 = 0;
-        gload(k, c0);
+    int st = grp;  // this group's steps: grp, grp + 2, ...
+    if (st < n_steps) {
+        gload(st);
         sstore(0);
-        __syncthreads();
+        f32_group_sync(grp);
         for (int b = 0;; b ^= 1) {
-            // the next step: next channel slice of this tap, else the next valid tap
-            int nk = k, nc = c0 + F32_BK;
-            if (nc >= cin) {
-                m &= m - 1;
-                nk = m ? __ffs(m) - 1 : -1;
-                nc = 0;
-            }
-            if (nk >= 0) gload(nk, nc);
+            const int nst = st + 2;
+            if (nst < n_steps) gload(nst);
+            float(*A)[F32_BM] = stage[grp][b][0];
+            float(*B)[F32_BN] = stage[grp][b][1];
+            // fragments of channel kk + 1 are read while channel kk's 64 FMAs run
+            float4 fa0 = *reinterpret_cast<const float4*>(&A[0][ty * 4]);
+            float4 fa1 = *reinterpret_cast<const float4*>(&A[0][32 + ty * 4]);
+            float4 fb0 = *reinterpret_cast<const float4*>(&B[0][tx * 4]);
+            float4 fb1 = *reinterpret_cast<const float4*>(&B[0][32 + tx * 4]);
 #pragma unroll
             for (int kk = 0; kk < F32_BK; ++kk) {
-                const float4 a0 = *reinterpret_cast<const float4*>(&As[b][kk][ty * 8]);
-                const float4 a1 = *reinterpret_cast<const float4*>(&As[b][kk][ty * 8 + 4]);
-                const float4 b0 = *reinterpret_cast<const float4*>(&Bs[b][kk][tx * 8]);
-                const float4 b1 = *reinterpret_cast<const float4*>(&Bs[b][kk][tx * 8 + 4]);
-                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                const float av[8] = {fa0.x, fa0.y, fa0.z, fa0.w, fa1.x, fa1.y, fa1.z, fa1.w};
+                const float bv[8] = {fb0.x, fb0.y, fb0.z, fb0.w, fb1.x, fb1.y, fb1.z, fb1.w};
+                if (kk + 1 < F32_BK) {
+                    fa0 = *reinterpret_cast<const float4*>(&A[kk + 1][ty * 4]);
+                    fa1 = *reinterpret_cast<const float4*>(&A[kk + 1][32 + ty * 4]);
+                    fb0 = *reinterpret_cast<const float4*>(&B[kk + 1][tx * 4]);
+                    fb1 = *reinterpret_cast<const float4*>(&B[kk + 1][32 + tx * 4]);
+                }
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
 #pragma unroll
                     for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
             }
-            if (nk < 0) break;
+            if (nst >= n_steps) break;
             sstore(b ^ 1);
-            __syncthreads();
-            k = nk;
-            c0 = nc;
+            f32_group_sync(grp);
+            st = nst;
         }
+    }
+
+    // group 1's partial sums -> group 0 (through group 1's stage buffers: 64 x 64 floats)
+    __syncthreads();
+    float(*part)[F32_BN] = reinterpret_cast<float(*)[F32_BN]>(&stage[1][0][0][0][0]);
+    if (grp == 1) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int rr = i < 4 ? ty * 4 + i : 32 + ty * 4 + (i - 4);
+            *reinterpret_cast<float4*>(&part[rr][tx * 4]) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            *reinterpret_cast<float4*>(&part[rr][32 + tx * 4]) =
+                make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+        }
+    }
+    __syncthreads();
+    if (grp == 1) return;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int rr = i < 4 ? ty * 4 + i : 32 + ty * 4 + (i - 4);
+        const float4 p0 = *reinterpret_cast<const float4*>(&part[rr][tx * 4]);
+        const float4 p1 = *reinterpret_cast<const float4*>(&part[rr][32 + tx * 4]);
+        acc[i][0] += p0.x;
+        acc[i][1] += p0.y;
+        acc[i][2] += p0.z;
+        acc[i][3] += p0.w;
+        acc[i][4] += p1.x;
+        acc[i][5] += p1.y;
+        acc[i][6] += p1.z;
+        acc[i][7] += p1.w;
     }
 
     // epilogue: bias, residual, scatter (as conv_simt_kernel)
@@ -284,7 +339,7 @@ __global__ void __launch_bounds__(F32_THREADS) conv_f32_tiled_kernel(
     const int wb = epi.row_map ? cout / epi.map_cols : cout;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        int64_t r = row0 + ty * 8 + i;
+        int64_t r = row0 + (i < 4 ? ty * 4 + i : 32 + ty * 4 + (i - 4));
         if (r >= n_rows) continue;
         if (epi.row_order) {
             r = epi.row_order[r];
@@ -292,7 +347,7 @@ __global__ void __launch_bounds__(F32_THREADS) conv_f32_tiled_kernel(
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int o = col0 + tx * 8 + j;
+            const int o = col0 + (j < 4 ? tx * 4 + j : 32 + tx * 4 + (j - 4));
             float v = acc[i][j] + (bias ? bias[o] : 0.f);
             if (res) v += load_residual<float>(res, epi.res_off, epi.res_rep, r, o, cout);
             int64_t orow = r;

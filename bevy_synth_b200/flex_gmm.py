@@ -25,6 +25,7 @@ plumbing); every computation runs in libsparseconv.  Errors are raised as
 from __future__ import annotations
 
 import ctypes
+import functools
 from dataclasses import dataclass, field
 
 import torch
@@ -49,15 +50,16 @@ class SparseSubmConvConfig:
     axis_sign: tuple = (1, 1, 1)
 
     def __post_init__(self):
+        object.__setattr__(self, "axis_order", tuple(self.axis_order))
+        object.__setattr__(self, "axis_sign", tuple(self.axis_sign))
         if self.in_channels_per_group is None:
             object.__setattr__(self, "in_channels_per_group", self.in_channels // max(self.groups, 1))
         if self.out_channels_per_group is None:
             object.__setattr__(self, "out_channels_per_group", self.out_channels // max(self.groups, 1))
 
     def c(self) -> ScConvConfig:
-        return ScConvConfig(self.in_channels, self.out_channels, self.kernel_d, self.kernel_h, self.kernel_w,
-                            self.in_channels_per_group, self.out_channels_per_group, self.groups,
-                            (ctypes.c_int32 * 3)(*self.axis_order), (ctypes.c_int32 * 3)(*self.axis_sign))
+        """The C struct (built once per distinct config; callers pass it by reference only)."""
+        return _config_struct(self)
 
     @staticmethod
     def subm3(in_channels: int, out_channels: int) -> "SparseSubmConvConfig":
@@ -66,11 +68,22 @@ class SparseSubmConvConfig:
         return SparseSubmConvConfig(in_channels, out_channels)
 
 
-def kernel_rows(config: SparseSubmConvConfig) -> int:
+@functools.lru_cache(maxsize=512)
+def _config_struct(config: SparseSubmConvConfig) -> ScConvConfig:
+    return ScConvConfig(config.in_channels, config.out_channels, config.kernel_d, config.kernel_h, config.kernel_w,
+                        config.in_channels_per_group, config.out_channels_per_group, config.groups,
+                        (ctypes.c_int32 * 3)(*config.axis_order), (ctypes.c_int32 * 3)(*config.axis_sign))
+
+
+@functools.lru_cache(maxsize=512)
+def _kernel_rows_cached(config: SparseSubmConvConfig) -> int:
     v = ctypes.c_int64(0)
-    c = config.c()
-    check(lib().sc_kernel_rows(ctypes.byref(c), ctypes.byref(v)))
+    check(lib().sc_kernel_rows(ctypes.byref(config.c()), ctypes.byref(v)))
     return v.value
+
+
+def kernel_rows(config: SparseSubmConvConfig) -> int:
+    return _kernel_rows_cached(config)
 
 
 def kernel_offsets(config: SparseSubmConvConfig) -> torch.Tensor:
