@@ -171,7 +171,16 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
         tile_n = (int)(cout <= 512 ? cout : W);
         if (tile_n % W != 0 || cout % tile_n != 0) return false;
     } else {
-        int64_t n_tiles = (cout + 255) / 256;
+        // Column tiles up to 512 wide for multi-tap convs: every column tile gathers the
+        // tile's rows again, and the gather, not the tensor pipe, bounds these convs, so
+        // one wide tile with a single-buffered accumulator beats two double-buffered ones
+        // (measured: 384->384 808 -> 550 us, 512->512 1158 -> 1048 us on config 2's grid).
+        // 1x1 convs keep 256 (they are epilogue-bound and need the epilogue overlap).
+        // SC_TC_WIDE=0|1 pins the choice.
+        const char* wide_env = std::getenv("SC_TC_WIDE");
+        const bool wide = wide_env ? wide_env[0] == '1' : K > 1;
+        const int64_t cap = wide ? 512 : 256;
+        int64_t n_tiles = (cout + cap - 1) / cap;
         while (cout % n_tiles != 0 || (cout / n_tiles) % 32 != 0) ++n_tiles;
         tile_n = (int)(cout / n_tiles);
     }

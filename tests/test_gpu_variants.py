@@ -1,11 +1,11 @@
 """Tuning variants of the tensor-core conv kernel give the default path's results.
 
-The launcher reads its tuning switches (SC_TC_*) once per process, so each
+The launcher reads some tuning switches (SC_TC_*) once per process, so each
 variant runs in a child process on the same seeded inputs and writes its
 outputs to a file; the parent compares them with the default variant's.  The
 variants change scheduling and copy engines only (4 or 8 gather warps, TMA
-row gathers, CTA pairs on or off, a persistent static schedule), never the order of the
-fp32 accumulation, so the comparison bound is tight.
+row gathers, CTA pairs on or off, a persistent static schedule, 256-wide
+column tiles), never the order of the fp32 accumulation, so the comparison bound is tight.
 """
 import os
 import subprocess
@@ -25,7 +25,7 @@ dev = torch.device("cuda:0")
 coords = torch.as_tensor(synth.config1(0).coords, device=dev)
 out = {}
 rng = np.random.default_rng(5)
-for cin, cout, sched in ((64, 64, True), (128, 256, True), (64, 96, False)):
+for cin, cout, sched in ((64, 64, True), (128, 256, True), (64, 96, False), (128, 384, True)):
     cfg = F.SparseSubmConvConfig.subm3(cin, cout)
     nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, coords)
     n = coords.shape[0]
@@ -47,12 +47,13 @@ VARIANTS = {
     "no_cta_pair": {"SC_TC_PAIR": "0"},
     "cta_pair_eight_gather_warps": {"SC_TC_PAIR": "1", "SC_TC_PW": "8"},
     "static_schedule": {"SC_TC_STATIC": "1"},
+    "narrow_column_tiles": {"SC_TC_WIDE": "0"},
 }
 
 
 def _run(tmp_path, name, env_extra):
     env = dict(os.environ)
-    for k in ("SC_TC_PW", "SC_TC_GATHER4", "SC_TC_PAIR", "SC_TC_STATIC"):
+    for k in ("SC_TC_PW", "SC_TC_GATHER4", "SC_TC_PAIR", "SC_TC_STATIC", "SC_TC_WIDE"):
         env.pop(k, None)
     env.update(env_extra)
     path = str(tmp_path / f"{name}.npz")
