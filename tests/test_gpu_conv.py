@@ -404,3 +404,26 @@ def test_pair_and_single_cta_kernels_agree(cuda_device, monkeypatch, cin, cout, 
     for a, s in zip(pair, single):
         assert rel_l2(a.numpy(), s.numpy()) <= 1e-6
     assert_no_fault()
+
+
+@pytest.mark.parametrize("channels,dtype", [(256, BF16), (512, BF16), (768, BF16), (1024, BF16), (96, BF16),
+                                            (256, torch.float32)])
+def test_layer_norm_act_rows(cuda_device, channels, dtype):
+    """LayerNorm(+affine) -> SiLU, LayerNorm alone and SiLU alone over rows: the bf16
+    rows of 256..1024 channels take the register-resident kernel, the rest the generic one."""
+    rng = np.random.default_rng(channels)
+    n = 1000
+    x = (rng.standard_normal((n, channels)) * 2 + 0.5).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(channels)).astype(np.float32)
+    be = (0.1 * rng.standard_normal(channels)).astype(np.float32)
+    xd = to_dev(x, dtype)
+    xr = xd.float().cpu().numpy()
+    tol = 1e-2 if dtype == BF16 else 1e-5
+    got = F.layer_norm_affine_silu_forward(xd, to_dev(g), to_dev(be), 1e-5).float().cpu().numpy()
+    assert rel_l2(got, oracle.silu(oracle.layer_norm(xr, g, be, 1e-5))) <= tol
+    got = F.layer_norm_affine_forward(xd, None, None, 1e-6).float().cpu().numpy()
+    assert rel_l2(got, oracle.layer_norm(xr, np.ones(channels, np.float32), np.zeros(channels, np.float32),
+                                         1e-6)) <= tol
+    got = F.silu_forward(xd).float().cpu().numpy()
+    assert rel_l2(got, oracle.silu(xr)) <= tol
+    assert_no_fault()
