@@ -362,77 +362,6 @@ __global__ void __launch_bounds__(F32_THREADS) conv_f32_tiled_kernel(
     }
 }
 
-// bf16 rows of 256*M channels (M = 1..4), dense, 16-byte aligned: a warp per row
-// holds the row in registers (M 16-byte loads a lane), so the row is read from
-// memory once for the mean, the variance and the output (the generic kernel
-// below reads it three times).  Same statistics: mean, then the biased variance
-// sum((x-mean)^2)/C, inv_std = 1/sqrt(var + eps).
-template <int M>
-__global__ void __launch_bounds__(256) rows_norm_act_bf16_vec_kernel(
-    const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t rows,
-    const float* __restrict__ gamma, const float* __restrict__ beta, float eps, int do_ln, int do_silu) {
-    constexpr int C = 256 * M;
-    const int lane = threadIdx.x & 31;
-    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (r >= rows) return;
-    const uint4* xr = reinterpret_cast<const uint4*>(x + r * C);
-    uint4* yr = reinterpret_cast<uint4*>(y + r * C);
-    float v[M][8];
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-        const uint4 u = __ldg(xr + m * 32 + lane);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            v[m][2 * e] = f.x;
-            v[m][2 * e + 1] = f.y;
-        }
-    }
-    float mean = 0.f, rstd = 1.f;
-    if (do_ln) {
-        float s = 0.f;
-#pragma unroll
-        for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) s += v[m][e];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        mean = s / (float)C;
-        float q = 0.f;
-#pragma unroll
-        for (int m = 0; m < M; ++m)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float d = v[m][e] - mean;
-                q += d * d;
-            }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-        rstd = 1.0f / sqrtf(q / (float)C + eps);
-    }
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-        const int c0 = (m * 32 + lane) * 8;
-        float a[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            a[e] = v[m][e];
-            if (do_ln) {
-                a[e] = (a[e] - mean) * rstd;
-                if (gamma) a[e] *= __ldg(gamma + c0 + e);
-                if (beta) a[e] += __ldg(beta + c0 + e);
-            }
-            if (do_silu) a[e] = silu_f(a[e]);
-        }
-        uint4 u;
-        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(a[2 * e], a[2 * e + 1]);
-        yr[m * 32 + lane] = u;
-    }
-}
-
 // Row-wise LayerNorm (+affine) and/or SiLU, one warp per entry.  Entry e is
 // the `width` values at element offset row*ld with row = map[e] (or e when
 // map is null; skipped when negative).  Two-pass statistics as the reference

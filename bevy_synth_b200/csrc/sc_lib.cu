@@ -779,19 +779,7 @@ int sc_layer_norm_act(sc_dtype dtype, const void* x, int64_t rows, int64_t chann
         rows_norm_act_kernel<float><<<grid1d(rows * 32, 256), 256, 0, st>>>(
             static_cast<const float*>(x), static_cast<float*>(y), rows, (int)channels, channels, nullptr,
             gamma, beta, eps, ln, silu);
-    else if (channels % 256 == 0 && channels <= 1024 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
-             reinterpret_cast<uintptr_t>(y) % 16 == 0) {
-        // the row held in registers (one read of it); 256..1024 channels
-        const auto* xb = static_cast<const __nv_bfloat16*>(x);
-        auto* yb = static_cast<__nv_bfloat16*>(y);
-        const unsigned g = grid1d(rows * 32, 256);
-        switch (channels / 256) {
-            case 1: rows_norm_act_bf16_vec_kernel<1><<<g, 256, 0, st>>>(xb, yb, rows, gamma, beta, eps, ln, silu); break;
-            case 2: rows_norm_act_bf16_vec_kernel<2><<<g, 256, 0, st>>>(xb, yb, rows, gamma, beta, eps, ln, silu); break;
-            case 3: rows_norm_act_bf16_vec_kernel<3><<<g, 256, 0, st>>>(xb, yb, rows, gamma, beta, eps, ln, silu); break;
-            default: rows_norm_act_bf16_vec_kernel<4><<<g, 256, 0, st>>>(xb, yb, rows, gamma, beta, eps, ln, silu); break;
-        }
-    } else
+    else
         rows_norm_act_kernel<__nv_bfloat16><<<grid1d(rows * 32, 256), 256, 0, st>>>(
             static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), rows, (int)channels,
             channels, nullptr, gamma, beta, eps, ln, silu);

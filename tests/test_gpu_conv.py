@@ -409,8 +409,8 @@ def test_pair_and_single_cta_kernels_agree(cuda_device, monkeypatch, cin, cout, 
 @pytest.mark.parametrize("channels,dtype", [(256, BF16), (512, BF16), (768, BF16), (1024, BF16), (96, BF16),
                                             (256, torch.float32)])
 def test_layer_norm_act_rows(cuda_device, channels, dtype):
-    """LayerNorm(+affine) -> SiLU, LayerNorm alone and SiLU alone over rows: the bf16
-    rows of 256..1024 channels take the register-resident kernel, the rest the generic one."""
+    """LayerNorm(+affine) -> SiLU, LayerNorm alone and SiLU alone over rows (the row
+    kernel the decoder blocks run before their first conv), bf16 and fp32."""
     rng = np.random.default_rng(channels)
     n = 1000
     x = (rng.standard_normal((n, channels)) * 2 + 0.5).astype(np.float32)
