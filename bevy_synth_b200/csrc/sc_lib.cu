@@ -214,7 +214,9 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     if (stg_env && std::atoi(stg_env) == 64) {
         stg = tc_stg_cols(tile_n, 64);
         S = deepest(stg);
-    } else if (!stg_env) {
+    } else if (!stg_env && K > 1) {
+        // (1x1 convs keep 128-column staging: they are epilogue-bound, and half as many staging
+        // rounds beat the TMA epilogue and the extra stage there: ConvNeXt stage 1.136 -> 1.075 ms)
         const int stg64 = tc_stg_cols(tile_n, 64);
         const int s64 = deepest(stg64);
         if (s64 >= S) {  // ties take 64 columns: the TMA (scatter4 / gather4) epilogue needs them
