@@ -219,7 +219,10 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
         // rounds beat the TMA epilogue and the extra stage there: ConvNeXt stage 1.136 -> 1.075 ms)
         const int stg64 = tc_stg_cols(tile_n, 64);
         const int s64 = deepest(stg64);
-        if (s64 >= S) {  // ties take 64 columns: the TMA (scatter4 / gather4) epilogue needs them
+        // ties take 64 columns, which the TMA (scatter4 / gather4) epilogue needs; a tile whose
+        // width 64 does not divide (e.g. 96) keeps the wider staging: fewer staging rounds beat the
+        // extra stage (config 3 level 2, C=96: 4.66 -> 4.48 ms)
+        if (s64 >= S && stg64 == 64) {
             stg = stg64;
             S = s64;
         }
