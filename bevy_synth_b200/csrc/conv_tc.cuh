@@ -24,10 +24,11 @@
 //   warps 0-3          epilogue: thread i owns TMEM lane / tile row i; output
 //                      and residual rows move through padded smem staging so
 //                      that global accesses are whole coalesced rows;
-//   warps 4..4+PW-1    A gather producers, one per SM sub-partition; each
-//                      reads its rows' map block one tile ahead; warp 4 lane 0
-//                      also issues the weight TMA and the launch-control
-//                      requests;
+//   warps 4..4+PW-1    A gather producers (PW = 4 or 8: one or two per SM
+//                      sub-partition); each reads its rows' map block one tile
+//                      ahead; the weight TMA of a stage is issued by one
+//                      producer lane in rotation (warp 4 in the full instance),
+//                      the launch-control requests by warp 4 lane 0;
 //   warp 4+PW          MMA warp: the whole warp runs the loop, one elected
 //                      lane issues tcgen05.mma and the commits.
 // Optionally (SC_TC_GATHER4=1) A rows arrive by TMA tile::gather4 instead of
@@ -35,7 +36,8 @@
 // The accumulator is double-buffered in TMEM (2 x 256 columns) when
 // tile_n <= 256, so the epilogue of one tile overlaps the MMAs of the next.
 //
-// PAIR (2-SM) variant (opt-in, SC_TC_PAIR=1; persistent grid with static
+// PAIR (2-SM) variant (the default for multi-tap convs with Cin, Cout <= 64;
+// SC_TC_PAIR=0|1 turns it off / on elsewhere; persistent grid with static
 // round-robin tiles), launched as clusters of two CTAs: a tile is 256 rows,
 // 128 per CTA; the leader issues tcgen05.mma.cta_group::2 with M = 256, each
 // CTA's A from its own shared memory and B split by N across the pair, so a
@@ -294,7 +296,7 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
     uint64_t* mask_bar = sched_empty + TC_SCHED;           // every producer warp posted its tap mask
     uint64_t* pair_bar = mask_bar + 1;                     // PAIR: the peer CTA's tap mask arrived
     uint64_t* res_bar = pair_bar + 1;                      // [4] per epilogue warp: staged residual rows landed
-    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(res_bar + 4);  // [S] PAIR relay: last step of a tile
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(res_bar + 4);  // [S] 2 = a tile's last step (bookkeeping, not read)
     uint32_t* tile_steps = stage_flags + S;  // [8] reduction steps per tile, ring over tiles
     // (the producers run at most S <= 8 stages, so at most 8 one-step tiles, ahead of the MMA thread)
     uint32_t* misc = tile_steps + 8;      // [0] tmem base, [1] abort

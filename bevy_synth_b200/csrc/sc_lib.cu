@@ -108,8 +108,8 @@ struct TcPlan {
     size_t smem;
 };
 
-// The CTA-pair (2-SM) kernel is opt-in (SC_TC_PAIR=1) until it is the faster
-// one on the measured workloads; the single-CTA kernel is the default.
+// SC_TC_STATIC=1: the single-CTA kernel on a persistent grid with round-robin tiles instead of
+// cluster launch control.
 static bool use_static_schedule() {
     static const bool v = [] {
         const char* e = std::getenv("SC_TC_STATIC");
