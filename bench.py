@@ -1,23 +1,36 @@
 """Benchmark of the sparse submanifold convolution path on B200.
 
-Workload (N=1): BASELINE config 2 -- a stack of 4 SparseResBlock3d at C=256,
-bf16, on a 128^3 union of 4 ellipsoid shells (seed = rank, one independent
-asset per GPU).  One step = neighbor map build from the coordinates + the
-first LN1/SiLU + 8 fused tcgen05 convs (conv1: +bias, LN2, SiLU; conv2:
-+bias, +residual, next block's LN1/SiLU as a second output).
+Default workload (every N): BASELINE config 5, the largest configuration that
+fits one GPU -- a 1024^3 union of 32 ellipsoid shells (7,067,536 voxels,
+seed 0) through SubM 64->64, 64->256, 256->256, 256->256 in bf16.  At N > 1 the
+same grid is cut into N Morton row ranges, one per GPU, and every layer
+exchanges its halo rows over NCCL (strong scaling: total work fixed).
+``--workload cfg4|cfg2|cfg3|cfg1|convnext`` runs another configuration
+(bevy_synth_b200/workloads.py).
+
+A step is one forward pass of the workload's conv layers.  The neighbor map,
+its conv schedule and (N > 1) the halo plan are built once per grid at set-up,
+as the reference caches its maps per grid; their device time is reported in
+``config.setup_ms``.
 
 metric  = sparse-conv voxel-outputs/s (sum over conv layers of N_out / time),
           with TFLOP/s (algorithmic 2*P*Cin*Cout, P = valid neighbor pairs) and
           the fraction of the measured bf16 peak alongside.
 value   = inputs resident in HBM, L2 flushed (256 MiB write) before every
-          step, each step timed with CUDA events on the launching stream.
+          step, steps timed with CUDA events on the launching stream; max of
+          the time over ranks, units summed over ranks.
 e2e     = the same through the public API with pinned host buffers: every
-          step copies its coordinates and features in (H2D) and its output
-          features out (D2H); steps are pipelined over H2D / compute / D2H
-          streams with two buffer slots, timed from the first H2D to the
-          last D2H.
---impl reference: the reference's CPU path (burn_flex_gmm's flex
-          gather+SGEMM, restated in oracle/) on the host cores.
+          step copies its input features in (H2D) and its output features out
+          (D2H), pipelined over H2D / compute / D2H streams with two buffer
+          slots, timed from the first H2D to the last D2H.
+roofline = the conv kernel (conv_tc_kernel): the step's algorithmic FLOPs over
+          the CUDA-event time of its conv launches, against the measured bf16
+          peak (MEASURED_PEAKS.json, burst).
+cpu_baseline = the reference's CPU path (burn_flex_gmm's flex gather+SGEMM,
+          restated in oracle/) on a Morton-contiguous window of the same grid,
+          every layer of the workload, on all host cores and on one core.
+--impl reference: the same CPU path and sample as cpu_baseline, one sample
+          round per step, on all host cores (rank 0 only).
 """
 from __future__ import annotations
 
@@ -34,19 +47,22 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_FLUSH_BYTES = 256 << 20
+CPU_ROWS_PER_CALL = 8192
+CPU_WINDOW_ROWS = 65536
 
 
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
-    return 1590.0, 6650.0, "fallback"
+        return (d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained"), d.get("hbm_gbs", 6650.0),
+                "measured")
+    return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def read_traffic():
-    """DRAM bytes per conv launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "conv_tc_cfg2_traffic.txt")
+def read_traffic(workload: str):
+    """DRAM bytes per conv launch (ncu) from the committed profile summary, if any."""
+    p = os.path.join(ROOT, "profiles", f"conv_tc_{workload}_traffic.txt")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -105,81 +121,151 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def cpu_sample(wl, seconds: float, threads: int, rows_per_step: int = 8192):
-    """Times the oracle's flex conv (the reference's CPU path) on Morton-
-    contiguous row slices of the workload's first C=256 layer."""
-    import oracle
+# ------------------------------------------------------------------ CPU sample
+class CpuSample:
+    """The reference's CPU conv path (burn_flex_gmm flex gather + SGEMM,
+    lib.rs:242-375, restated in oracle/) on a Morton-contiguous window of the
+    workload's grid: the window's rows, their neighbor map against the grid
+    cells around them, and every conv layer of the workload, in slices of
+    CPU_ROWS_PER_CALL rows.  Features are seeded N(0, 1) (the CPU's values do
+    not change its speed)."""
 
-    c = wl.feats.shape[1]
-    cfg = oracle.OracleConfig(c, c)
-    nbr = oracle.build_neighbor_rows(cfg, wl.coords.astype(np.uint32), oracle.DUP_LOWEST)
-    packed = oracle.pack_flex_weight(cfg, wl.params[0]["w1"])
-    n = nbr.shape[0]
-    done, pairs, t0 = 0, 0, time.perf_counter()
-    start = 0
-    while True:
-        rows = slice(start, min(start + rows_per_step, n))
-        oracle.subm_conv_flex(cfg, wl.params[0]["w1"], wl.params[0]["b1"], wl.feats, nbr[rows], packed=packed,
-                              threads=threads)
-        done += rows.stop - rows.start
-        pairs += int((nbr[rows] >= 0).sum())
-        start = rows.stop % n
-        if time.perf_counter() - t0 >= seconds:
-            break
-    dt = time.perf_counter() - t0
-    return done / dt, 2.0 * pairs * c * c / dt / 1e12, done
+    def __init__(self, coords: np.ndarray, layers: list, window: int = CPU_WINDOW_ROWS):
+        import oracle
+
+        self.oracle = oracle
+        n = coords.shape[0]
+        w = min(window, n)
+        a = max(0, n // 2 - w // 2)
+        self.window = coords[a:a + w]
+        lo = self.window[:, 1:].min(0) - 1
+        hi = self.window[:, 1:].max(0) + 1
+        inb = np.all((coords[:, 1:] >= lo) & (coords[:, 1:] <= hi), axis=1) & np.isin(coords[:, 0],
+                                                                                   np.unique(self.window[:, 0]))
+        cand = np.ascontiguousarray(coords[inb])
+        cfg0 = oracle.OracleConfig(1, 1)
+        self.nbr = oracle.build_neighbor_rows(cfg0, cand.astype(np.uint32), oracle.DUP_LOWEST,
+                                              self.window.astype(np.uint32))
+        rng = np.random.default_rng(7)
+        self.layers = []
+        for cin, cout, wt, b in layers:
+            cfg = oracle.OracleConfig(cin, cout)
+            x = rng.standard_normal((cand.shape[0], cin)).astype(np.float32)
+            self.layers.append((cfg, np.asarray(wt, np.float32), np.asarray(b, np.float32), x,
+                                oracle.pack_flex_weight(cfg, wt)))
+        self.pos = 0
+        self.desc = (f"{w} Morton-contiguous rows of the grid (rows {a}..{a + w}), their neighbor map, "
+                     f"{len(layers)} conv layer(s) "
+                     f"{[f'{c.in_channels}->{c.out_channels}' for c, *_ in self.layers]} in slices of "
+                     f"{CPU_ROWS_PER_CALL} rows")
+
+    def round(self, threads: int) -> tuple[int, float]:
+        """One slice through every layer: (voxel outputs, seconds)."""
+        w = self.nbr.shape[0]
+        s = self.pos
+        rows = slice(s, min(s + CPU_ROWS_PER_CALL, w))
+        self.pos = rows.stop % w
+        t0 = time.perf_counter()
+        for cfg, wt, b, x, packed in self.layers:
+            self.oracle.subm_conv_flex(cfg, wt, b, x, self.nbr[rows], packed=packed, threads=threads)
+        return (rows.stop - rows.start) * len(self.layers), time.perf_counter() - t0
+
+    def rate(self, seconds: float, threads: int) -> tuple[float, float]:
+        """Voxel-outputs/s over whole rounds lasting about ``seconds``."""
+        units, spent = 0, 0.0
+        while spent < seconds:
+            u, dt = self.round(threads)
+            units += u
+            spent += dt
+        return units / spent, spent
 
 
 def run_reference(args, rank: int, world: int):
+    """The reference arm: the reference's CPU path on the host cores, same
+    workload and sample as cpu_baseline, one sample round per step."""
     if rank != 0:
         return
     from bevy_synth_b200 import synth
 
-    wl = synth.config2(0)
+    wl_name = args.workload
+    if wl_name == "cfg5":
+        coords = synth.config5_coords(0)
+        p = synth.config5_params(0)
+        layers = [(ci, co, w, b) for (ci, co), w, b in zip(p["chans"], p["w"], p["b"])]
+        name = "cfg5_sharded_grid_bf16"
+    elif wl_name == "cfg4":
+        wl = synth.config4(0, feats=False)
+        coords, layers, name = wl.coords, [(512, 512, wl.params["w"][0], wl.params["b"][0])], wl.name
+    elif wl_name == "cfg2":
+        wl = synth.config2(0)
+        coords, layers, name = wl.coords, [(256, 256, wl.params[0]["w1"], wl.params[0]["b1"])], wl.name
+    elif wl_name == "cfg1":
+        wl = synth.config1(0)
+        coords, layers, name = wl.coords, [(64, 64, wl.params["w"], wl.params["b"])], wl.name
+    else:
+        print(json.dumps({"impl": "reference", "unavailable": f"no CPU sample defined for {wl_name}"}))
+        return
     threads = os.cpu_count() or 1
-    # each step: one bounded slice of the config-2 C=256 layer
-    import oracle
-
-    c = wl.feats.shape[1]
-    cfg = oracle.OracleConfig(c, c)
-    nbr = oracle.build_neighbor_rows(cfg, wl.coords.astype(np.uint32), oracle.DUP_LOWEST)
-    packed = oracle.pack_flex_weight(cfg, wl.params[0]["w1"])
-    rows_per_step = 4096
-    times, rows_done = [], 0
+    cs = CpuSample(coords, layers)
+    times, units = [], 0
     for i in range(args.warmup + args.steps):
-        s = (i * rows_per_step) % nbr.shape[0]
-        sl = slice(s, min(s + rows_per_step, nbr.shape[0]))
-        t0 = time.perf_counter()
-        oracle.subm_conv_flex(cfg, wl.params[0]["w1"], wl.params[0]["b1"], wl.feats, nbr[sl], packed=packed,
-                              threads=threads)
-        dt = time.perf_counter() - t0
+        u, dt = cs.round(threads)
         if i >= args.warmup:
             times.append(dt)
-            rows_done += sl.stop - sl.start
+            units += u
     total = sum(times)
-    v = rows_done / total
+    v = units / total
     line = {
         "impl": "reference", "metric": "sparse conv voxel-outputs/s", "value": v, "unit": "voxel-outputs/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name, "voxels": int(nbr.shape[0]), "channels": c,
-                   "sample": f"{rows_per_step} Morton-contiguous rows of one C=256 SubM layer per step"},
+        "higher_is_better": True, "scaling": "strong" if wl_name == "cfg5" else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": name, "voxels": int(coords.shape[0]), "sample": cs.desc},
         "cpu_baseline": {"value": v, "unit": "voxel-outputs/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows_per_step}-row slices of the config-2 C=256 layer; restatement of "
-                                   "burn_flex_gmm flex gather+SGEMM (reference Rust not buildable here)"},
+                         "sample": cs.desc + "; restatement of burn_flex_gmm flex gather+SGEMM "
+                                             "(the reference's Rust is not buildable here)"},
         "e2e": {"value": v, "unit": "voxel-outputs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ GPU arm
+class LaunchTimer:
+    """Conv-launch observer (flex_gmm.set_conv_observer): CUDA events around
+    every conv launch on the launching stream."""
+
+    def __init__(self):
+        import torch
+
+        self.torch = torch
+        self.events = []
+        self._open = None
+
+    def before(self, config, n_rows):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record()
+        self._open = (config, n_rows, e)
+
+    def after(self, config, n_rows):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record()
+        cfg, rows, e0 = self._open
+        self.events.append((f"{cfg.in_channels}->{cfg.out_channels}", rows, e0, e))
+
+    def times(self):
+        return [(lbl, rows, a.elapsed_time(b)) for lbl, rows, a, b in self.events]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg4", "cfg2", "cfg3", "cfg1", "convnext"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -194,201 +280,164 @@ def main():
     import torch
     import torch.distributed as dist
 
-    from bevy_synth_b200 import _lib, blocks, synth
+    from bevy_synth_b200 import _lib
     from bevy_synth_b200 import flex_gmm as F
+    from bevy_synth_b200.workloads import WORKLOADS
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-
-    wl = synth.config2(seed=rank)
-    c = 256
-    cfg = F.SparseSubmConvConfig.subm3(c, c)
-    stack = blocks.ResBlockStack([blocks.ResBlockParams.from_numpy(p, dev) for p in wl.params])
-    n = wl.coords.shape[0]
-    coords_d = torch.as_tensor(wl.coords, device=dev)
-    feats_d = torch.as_tensor(wl.feats, device=dev).to(torch.bfloat16)
-    ws = F.NeighborWorkspace(dev, n)
-    bufs: dict = {}
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    wl = WORKLOADS[args.workload](dev, rank, world)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    conv_events: list = []
 
-    use_order = os.environ.get("SC_ROW_ORDER", "1") == "1"
-
-    def step(coords_t, feats_t, record=False):
-        nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, coords_t, check_status=False, workspace=ws)
-        order = F.neighbor_schedule(cfg, nbr) if use_order else None
-        if record:
-            return stack_forward_timed(feats_t, nbr, order)
-        return stack.forward(feats_t, nbr, bufs, order), nbr
-
-    def stack_forward_timed(x, nbr, order):
-        # identical to ResBlockStack.forward, with events around each conv launch
-        b0 = stack.blocks[0]
-        h = F.layer_norm_affine_silu_forward(x, b0.ln1_g, b0.ln1_b, b0.eps, out=bufs["h"])
-        h1 = bufs["h1"]
-        ping = [bufs["x0"], bufs["x1"]]
-        cur = x
-        for i, p in enumerate(stack.blocks):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            F.sparse_subm_conv_forward(cfg, h, nbr, p.w1, p.b1, F.Epilogue(layer_norm=True, ln_eps=p.eps,
-                                       ln_gamma=p.ln2_g, ln_beta=p.ln2_b, silu=True, schedule=order), out=h1)
-            e1.record(stream)
-            conv_events.append((e0, e1))
-            nxt = ping[i % 2]
-            if i + 1 < len(stack.blocks):
-                q = stack.blocks[i + 1]
-                e = F.Epilogue(residual=cur, layer_norm=True, ln_eps=q.eps, ln_gamma=q.ln1_g, ln_beta=q.ln1_b,
-                               silu=True, out2=h, schedule=order)
-            else:
-                e = F.Epilogue(residual=cur, schedule=order)
-            e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e2.record(stream)
-            F.sparse_subm_conv_forward(cfg, h1, nbr, p.w2, p.b2, e, out=nxt)
-            e3.record(stream)
-            conv_events.append((e2, e3))
-            cur = nxt
-        return cur, nbr
-
-    # warm-up (also checks the map's status once)
-    for _ in range(args.warmup):
-        y, nbr = step(coords_d, feats_d)
-    ws.status(dev)
-    torch.cuda.synchronize()
-    P = int((nbr >= 0).sum().item())
-    convs = stack.conv_count()
-    flops_per_conv = 2.0 * P * c * c
-    assert torch.isfinite(y.float()).all().item(), "non-finite output"
-
-    # ---- device-resident timing ---------------------------------------------
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    sampler = ClockSampler(local)
-    step_ms = []
+    # ---- warm-up ---------------------------------------------------------------
+    for _ in range(args.warmup):
+        y = wl.step(0)
     barrier()
+    assert _lib.device_fault() == 0, "device fault during warm-up"
+    assert bool(torch.isfinite(y.float()).all()), "non-finite output"
+
+    # ---- device-resident timing ------------------------------------------------
+    timer = LaunchTimer()
+    sampler = ClockSampler(local)
+    steps = []
+    barrier()
+    F.set_conv_observer(timer)
     with sampler:
         for _ in range(args.steps):
             flush.zero_()
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s0.record(stream)
-            step(coords_d, feats_d, record=True)
+            wl.step(0)
             s1.record(stream)
-            step_ms.append((s0, s1))
+            steps.append((s0, s1))
         barrier()
-    t_dev = sum(a.elapsed_time(b) for a, b in step_ms) / 1e3
-    conv_ms = [a.elapsed_time(b) for a, b in conv_events]
+    F.set_conv_observer(None)
+    t_dev = sum(a.elapsed_time(b) for a, b in steps) / 1e3
+    launches = timer.times()
     assert _lib.device_fault() == 0, "device fault during the timed region"
 
-    # ---- end-to-end through the public API with host buffers -----------------
-    # Steps are pipelined over three streams (H2D, compute, D2H) and two slots
-    # of device inputs / outputs, so the copies of one step overlap the convs of
-    # its neighbours; every step still copies its inputs in and its result out.
-    # The time is the span from the first H2D to the last D2H.
-    coords_h = torch.as_tensor(wl.coords).pin_memory()
-    feats_h = torch.as_tensor(wl.feats).to(torch.bfloat16).pin_memory()
-    out_h = [torch.empty((n, c), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    cd = [torch.empty_like(coords_d) for _ in range(2)]
-    fd = [torch.empty((n, c), dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    slot_bufs = [dict(bufs), {}]
-    s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    in_free = [None, None]
-    out_free = [None, None]
+    # ---- end-to-end through the public API with host buffers --------------------
+    t_e2e, h2d, d2h = None, 0, 0
+    if not args.no_e2e:
+        host_in = [t.cpu().pin_memory() for t in wl.inputs(0)]
+        out0 = wl.output(0)
+        host_out = [torch.empty(out0.shape, dtype=out0.dtype).pin_memory() for _ in range(2)]
+        h2d = int(sum(t.numel() * t.element_size() for t in host_in))
+        d2h = int(out0.numel() * out0.element_size())
+        s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        in_free, out_free = [None, None], [None, None]
 
-    def e2e_step(i, first=None):
-        k = i % 2
-        with torch.cuda.stream(s_h2d):
-            if first is not None:
-                first.record(s_h2d)
-            if in_free[k] is not None:
-                s_h2d.wait_event(in_free[k])
-            cd[k].copy_(coords_h, non_blocking=True)
-            fd[k].copy_(feats_h, non_blocking=True)
-            h2d_done = torch.cuda.Event()
-            h2d_done.record(s_h2d)
-        stream.wait_event(h2d_done)
-        if out_free[k] is not None:
-            stream.wait_event(out_free[k])
-        flush.zero_()
-        nbr_k = F.neighbor_rows_tensor_from_coords_tensor(cfg, cd[k], check_status=False, workspace=ws)
-        order_k = F.neighbor_schedule(cfg, nbr_k) if use_order else None
-        y = stack.forward(fd[k], nbr_k, slot_bufs[k], order_k)
-        done = torch.cuda.Event()
-        done.record(stream)
-        in_free[k] = done
-        with torch.cuda.stream(s_d2h):
-            s_d2h.wait_event(done)
-            out_h[k].copy_(y, non_blocking=True)
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record(s_d2h)
-            out_free[k] = ev
-        return ev
+        def e2e_step(i, first=None):
+            k = i % 2
+            with torch.cuda.stream(s_h2d):
+                if first is not None:
+                    first.record(s_h2d)
+                if in_free[k] is not None:
+                    s_h2d.wait_event(in_free[k])
+                for hsrc, ddst in zip(host_in, wl.inputs(k)):
+                    ddst.copy_(hsrc, non_blocking=True)
+                h2d_done = torch.cuda.Event()
+                h2d_done.record(s_h2d)
+            stream.wait_event(h2d_done)
+            if out_free[k] is not None:
+                stream.wait_event(out_free[k])
+            flush.zero_()
+            y = wl.step(k)
+            done = torch.cuda.Event()
+            done.record(stream)
+            in_free[k] = done
+            with torch.cuda.stream(s_d2h):
+                s_d2h.wait_event(done)
+                host_out[k].copy_(y, non_blocking=True)
+                y.record_stream(s_d2h)
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(s_d2h)
+                out_free[k] = ev
+            return ev
 
-    for i in range(2):  # untimed: first use of both slots
-        e2e_step(i)
-    barrier()
-    e_first = torch.cuda.Event(enable_timing=True)
-    e_last = None
-    for i in range(args.steps):
-        e_last = e2e_step(i, e_first if i == 0 else None)
-    barrier()
-    t_e2e = e_first.elapsed_time(e_last) / 1e3
+        for i in range(2):  # untimed: first use of both slots
+            e2e_step(i)
+        barrier()
+        e_first = torch.cuda.Event(enable_timing=True)
+        e_last = None
+        for i in range(args.steps):
+            e_last = e2e_step(i, e_first if i == 0 else None)
+        barrier()
+        t_e2e = e_first.elapsed_time(e_last) / 1e3
+        assert _lib.device_fault() == 0, "device fault during the end-to-end leg"
 
-    # ---- max over ranks -------------------------------------------------------
-    units = float(n * convs * args.steps)
-    flops = flops_per_conv * convs * args.steps
-    vec = torch.tensor([t_dev, t_e2e, units, flops, n], dtype=torch.float64, device=dev)
+    # ---- max over ranks ---------------------------------------------------------
+    units = float(wl.units * args.steps)
+    flops = float(wl.flops * args.steps)
+    vec = torch.tensor([t_dev, t_e2e or 0.0, units, flops], dtype=torch.float64, device=dev)
     if world > 1:
         tmax = vec[:2].clone()
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
         tot = vec[2:].clone()
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        t_dev, t_e2e = float(tmax[0]), float(tmax[1])
-        units, flops, n_all = float(tot[0]), float(tot[1]), int(tot[2])
-    else:
-        n_all = n
+        t_dev, t_e2e = float(tmax[0]), (float(tmax[1]) if t_e2e is not None else None)
+        units, flops = float(tot[0]), float(tot[1])
 
     if rank == 0:
-        peak_tf, hbm, peak_kind = load_peaks()
-        avg_conv_s = float(np.mean(conv_ms)) / 1e3
-        achieved = flops_per_conv / avg_conv_s / 1e12
-        tflops = flops / t_dev / 1e12
+        peak_tf, peak_sus, hbm, peak_kind = load_peaks()
+        conv_ms_step = sum(t for _, _, t in launches) / args.steps
+        achieved = wl.flops / (conv_ms_step / 1e3) / 1e12
+        n_launch_step = len(launches) // args.steps
+        per_layer = []
+        lpl = getattr(wl, "launches_per_layer", 1)
+        flops_l = getattr(wl, "layer_flops", None)
+        for j in range(0, n_launch_step, lpl):
+            ms = sum(launches[s * n_launch_step + j + q][2] for s in range(args.steps)
+                     for q in range(lpl)) / args.steps
+            d = {"layer": launches[j][0], "ms": round(ms, 4)}
+            if flops_l is not None and j // lpl < len(flops_l):
+                tf = flops_l[j // lpl] / (ms / 1e3) / 1e12
+                d.update({"tflops": round(tf, 1), "frac_bf16_peak": round(tf / peak_tf, 4)})
+            per_layer.append(d)
         cpu = None
-        if world == 1 and not args.no_cpu:
+        if world == 1 and not args.no_cpu and wl.cpu_layers() is not None:
             threads = os.cpu_count() or 1
-            v, tf, rows = cpu_sample(wl, args.cpu_seconds, threads)
-            cpu = {"value": v, "unit": "voxel-outputs/s", "cores": threads, "kind": "port",
-                   "tflops": tf,
-                   "sample": f"{rows} rows of one C=256 SubM layer of this workload (Morton-contiguous slices, "
-                             f"~{args.cpu_seconds:.0f} s); oracle restatement of burn_flex_gmm flex gather+SGEMM"}
+            cs = CpuSample(wl.coords_np, wl.cpu_layers())
+            v_all, spent = cs.rate(args.cpu_seconds, threads)
+            v_one, spent1 = cs.rate(args.cpu_seconds / 3, 1)
+            cpu = {"value": v_all, "unit": "voxel-outputs/s", "cores": threads, "kind": "port",
+                   "sample": f"{cs.desc}; {spent:.1f} s on {threads} threads; oracle restatement of "
+                             "burn_flex_gmm flex gather+SGEMM (the reference's CPU path)",
+                   "single_thread": {"value": v_one, "cores": 1, "seconds": round(spent1, 1),
+                                     "note": "the reference's own configuration (matrixmultiply without "
+                                             "threading)"}}
+        cfgd = wl.describe()
+        cfgd.update({"l2": "flushed before every step (256 MiB write); inputs also larger than L2"
+                     if args.workload == "cfg5" else "flushed before every step (256 MiB write)",
+                     "conv_launches_per_step": n_launch_step, "per_layer": per_layer})
         line = {
             "metric": "sparse conv voxel-outputs/s", "value": units / t_dev, "unit": "voxel-outputs/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "tflops": tflops, "pct_bf16_peak": tflops / (peak_tf * world),
-            "config": {"workload": wl.name, "voxels_per_gpu": n, "voxels_total": n_all, "blocks": len(wl.params),
-                       "channels": c, "convs_per_step": convs, "valid_pairs_P": P,
-                       "step": "neighbor map + row order + LN1/SiLU + 8 fused SubM convs",
-                       "row_order": "mask-sorted" if use_order else "morton",
-                       "l2": "flushed before every step (256 MiB write); per-step CUDA events",
-                       "parallelism": f"asset-sharded x{world} (one independent asset per GPU, no collective)"},
+            "ms_per_step": 1e3 * t_dev / args.steps, "higher_is_better": True,
+            "scaling": "strong" if args.workload == "cfg5" else "weak",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded; BASELINE shapes and distributions)",
+            "tflops": flops / t_dev / 1e12, "pct_bf16_peak": flops / t_dev / 1e12 / (peak_tf * world),
+            "config": cfgd,
             "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
                          "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
-                         "peak_source": f"{peak_kind} bf16 (burst)", "traffic": read_traffic(),
-                         "flops_per_launch": flops_per_conv, "avg_launch_ms": avg_conv_s * 1e3},
+                         "frac_of_sustained": (achieved / peak_sus) if peak_sus else None,
+                         "peak_source": f"{peak_kind} bf16 (burst); frac_of_sustained against the sustained figure",
+                         "traffic": read_traffic(args.workload),
+                         "flops_per_step_rank0": wl.flops, "conv_ms_per_step_rank0": conv_ms_step},
             "cpu_baseline": cpu,
-            "e2e": {"value": units / t_e2e, "unit": "voxel-outputs/s",
-                    "h2d_bytes_per_step": int(coords_h.numel() * 4 + feats_h.numel() * 2),
-                    "d2h_bytes_per_step": int(out_h[0].numel() * 2)},
-            "gpu_launches": int(args.steps * (2 + (2 if use_order else 0) + 1 + convs)),
+            "e2e": ({"value": units / t_e2e, "unit": "voxel-outputs/s", "h2d_bytes_per_step": h2d * world,
+                     "d2h_bytes_per_step": d2h * world} if t_e2e else None),
+            "gpu_launches": int(args.steps * wl.kernels_per_step),
             "clocks": sampler.report(),
         }
         print(json.dumps(line), flush=True)

@@ -4,6 +4,7 @@
 """
 from __future__ import annotations
 
+import hashlib
 import os
 import subprocess
 import sys
@@ -12,7 +13,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 SRC = os.path.join(HERE, "csrc", "sc_lib.cu")
 OUT = os.path.join(HERE, "libsparseconv.so")
-DEPS = [os.path.join(HERE, "csrc", f) for f in sorted(os.listdir(os.path.join(HERE, "csrc")))] + [
+DEPS = [os.path.join(HERE, "csrc", f) for f in sorted(os.listdir(os.path.join(HERE, "csrc")))
+        if f.endswith((".cu", ".cuh", ".h"))] + [
     os.path.join(ROOT, "include", "sparseconv.h")]
 
 NVCC_FLAGS = [
@@ -30,11 +32,27 @@ def nvcc() -> str:
     return "nvcc"
 
 
+STAMP = OUT + ".srchash"
+
+
+def source_hash() -> str:
+    """SHA-256 over the compile command and every source the library is built from."""
+    h = hashlib.sha256()
+    h.update(" ".join(NVCC_FLAGS).encode())
+    for d in DEPS:
+        h.update(os.path.basename(d).encode())
+        with open(d, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
 def up_to_date() -> bool:
-    if not os.path.exists(OUT):
+    """True when the in-tree library was built by this module from exactly the
+    current sources (the hash written beside it at build time matches)."""
+    if not (os.path.exists(OUT) and os.path.exists(STAMP)):
         return False
-    t = os.path.getmtime(OUT)
-    return all(os.path.getmtime(d) <= t for d in DEPS if os.path.exists(d))
+    with open(STAMP) as f:
+        return f.read().strip() == source_hash()
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -42,6 +60,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return OUT
     cmd = [nvcc()] + NVCC_FLAGS + (["-Xptxas", "-v"] if verbose else []) + ["-o", OUT, SRC]
     subprocess.run(cmd, check=True)
+    with open(STAMP, "w") as f:
+        f.write(source_hash() + "\n")
     return OUT
 
 

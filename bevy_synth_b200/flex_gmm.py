@@ -309,10 +309,27 @@ def sparse_subm_conv_forward(config: SparseSubmConvConfig, input: torch.Tensor, 
             out = torch.empty((n_q, config.out_channels), dtype=input.dtype, device=input.device)
     c = config.c()
     ec = e.c()
+    obs = _CONV_OBSERVER
+    if obs is not None:
+        obs.before(config, n_q)
     check(lib().sc_subm_conv_forward(ctypes.byref(c), _DT[input.dtype], _ptr(input), input.shape[0],
                                      _ptr(neighbor_rows), n_q, _ptr(weight), _ptr(bias), ctypes.byref(ec),
                                      _ptr(out), _stream(input)))
+    if obs is not None:
+        obs.after(config, n_q)
     return out
+
+
+_CONV_OBSERVER = None
+
+
+def set_conv_observer(observer) -> None:
+    """Installs ``observer`` (or removes it, with None): its ``before(config,
+    n_rows)`` and ``after(config, n_rows)`` are called around every conv launch,
+    on the launching host thread, so that it can record CUDA events on the
+    current stream (per-launch device timing).  Changes no result."""
+    global _CONV_OBSERVER
+    _CONV_OBSERVER = observer
 
 
 def sparse_subm_conv_forward_cubecl(config: SparseSubmConvConfig, input: torch.Tensor,

@@ -10,13 +10,19 @@ Two partitions are built here:
 * Assets: independent grids, batch index in coord[0].
   Each rank takes a contiguous block of assets; no neighbor crosses a batch,
   so there is no data-path collective.
-* Morton ranges (config 5): one large grid, rows Morton-sorted, rank r owns
-  rows [lo_r, hi_r).  Every rank holds the (small) coordinate list, queries
-  its own rows against the whole grid, and a one-time plan exchanges the
-  requested boundary rows' ids.  Per layer each rank packs the rows others
-  need (sc_gather_rows) and one all_to_all delivers the halo rows into its
-  own [n_local + n_halo, C] buffer; the local neighbor map addresses halo rows
-  as ids >= n_local, which the conv accepts because query rows <= input rows.
+* Morton ranges (config 5): one large grid, rows sorted by (batch, Morton
+  code), rank r owns the r-th contiguous range.  A rank holds only its own
+  coordinates.  ``HaloPlan.build_local`` finds, from the rank's own rows, the
+  neighbor coordinates that fall in another rank's key range, asks their
+  owners (one all-to-all of coordinates, one of answers) and numbers the rows
+  that exist as halo rows n_local, n_local + 1, ...  Per layer each owner
+  packs the rows others read (sc_gather_rows) and one all-to-all delivers
+  them into the receiver's [n_local + n_halo, C] layer buffer; the local map
+  addresses halo rows as ids >= n_local, which the conv accepts because query
+  rows <= input rows.  Local rows are kept in plan order [interior | boundary]
+  (boundary = reads a halo row or is sent to a peer), so each layer runs the
+  interior rows while the exchange is in flight on a second stream and the
+  boundary rows after it.
 """
 from __future__ import annotations
 
@@ -45,8 +51,36 @@ def morton_ranges(n_rows: int, world: int) -> list[tuple[int, int]]:
     return out
 
 
-MapFn = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]  # (all coords, query coords) -> [n_q, K] global ids
+# ------------------------------------------------------------------ Morton keys
+_SPREAD = ((32, 0x1F00000000FFFF), (16, 0x1F0000FF0000FF), (8, 0x100F00F00F00F00F),
+           (4, 0x10C30C30C30C30C3), (2, 0x1249249249249249))
+
+
+def _spread3(v: torch.Tensor) -> torch.Tensor:
+    """Bit i of v (< 2^21) moved to bit 3i, int64."""
+    v = v.to(torch.int64) & 0x1FFFFF
+    for sh, mask in _SPREAD:
+        v = (v | (v << sh)) & mask
+    return v
+
+
+def morton_key(batch: torch.Tensor, xyz: torch.Tensor) -> torch.Tensor:
+    """Sort key of a coordinate: (batch << 48) | interleave(x, y, z), x in bit 0.
+    Components lie in [0, 65534], so the interleave fits 48 bits and the key
+    orders rows exactly as a (batch, Morton code) sort does."""
+    code = _spread3(xyz[:, 0]) | (_spread3(xyz[:, 1]) << 1) | (_spread3(xyz[:, 2]) << 2)
+    return (batch.to(torch.int64) << 48) | code
+
+
+QueryFn = Callable[[torch.Tensor, torch.Tensor, object], torch.Tensor]
 GatherFn = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+def _device_query(table: torch.Tensor, query: torch.Tensor, cfg) -> torch.Tensor:
+    """[n_query, K] rows of ``table`` at query + offset (the library's map)."""
+    from . import flex_gmm as F
+
+    return F.neighbor_rows_query_tensor(cfg, table, query)
 
 
 def _default_gather(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
@@ -57,58 +91,125 @@ def _default_gather(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
     return src.index_select(0, idx.to(torch.int64))
 
 
+def _kernel_offsets(cfg) -> torch.Tensor:
+    from . import flex_gmm as F
+
+    return F.kernel_offsets(cfg)
+
+
+def _point_config():
+    """The 1x1x1 config of a point lookup (offset 0)."""
+    from . import flex_gmm as F
+
+    return F.SparseSubmConvConfig(1, 1, 1, 1, 1)
+
+
 @dataclass
 class HaloPlan:
-    """Exchange plan of one rank for a Morton-range-sharded grid."""
+    """Exchange plan of one rank for a Morton-range-sharded grid.
+
+    Local rows are numbered in plan order: ``order[p]`` is the rank's own
+    (Morton-local) row at plan row p; rows [0, n_interior) read no halo row
+    and are sent to no peer, rows [n_interior, n_local) are the boundary."""
 
     rank: int
     world: int
-    lo: int
-    hi: int
+    lo: int                      # first global row of this rank
+    n_local: int
     n_halo: int
-    nbr_local: torch.Tensor      # [n_local, K] int32: own rows [0, n_local), halo rows [n_local, n_local + n_halo)
+    n_interior: int
+    order: torch.Tensor          # [n_local] int32: plan row -> Morton-local row
+    nbr_local: torch.Tensor      # [n_local, K] int32 in plan numbering; halo rows n_local + h
     halo_global: torch.Tensor    # [n_halo] int64 global ids, in receive order
-    send_idx: torch.Tensor       # [n_send] int32 local ids to pack, grouped by destination rank
+    send_idx: torch.Tensor       # [n_send] int32 plan rows to pack, grouped by destination rank
     send_counts: list
     recv_counts: list
     group: object = None
 
     @property
-    def n_local(self) -> int:
-        return self.hi - self.lo
+    def hi(self) -> int:
+        return self.lo + self.n_local
 
     @staticmethod
-    def build(coords_all: torch.Tensor, ranges: list, rank: int, map_fn: MapFn, group=None) -> "HaloPlan":
-        world = len(ranges)
-        lo, hi = ranges[rank]
-        dev = coords_all.device
-        g = map_fn(coords_all, coords_all[lo:hi].contiguous()).to(torch.int64)
-        valid = g >= 0
-        own = valid & (g >= lo) & (g < hi)
-        halo_mask = valid & ~own
-        halo_ids = torch.unique(g[halo_mask])                       # sorted == receive order
-        n_halo = int(halo_ids.numel())
-        local = torch.full_like(g, -1)
-        local[own] = g[own] - lo
-        local[halo_mask] = (hi - lo) + torch.searchsorted(halo_ids, g[halo_mask])
-        # requests per owner (contiguous ranges -> the sorted ids split by owner)
-        bounds = torch.tensor([r[1] for r in ranges], dtype=torch.int64, device=dev)
-        owner = torch.searchsorted(bounds, halo_ids, right=True)
-        req_counts = torch.bincount(owner, minlength=world).to(torch.int64)
-        cnt_in = torch.zeros(world, dtype=torch.int64, device=dev)
+    def build_local(coords_local: torch.Tensor, cfg, group=None, query_fn: QueryFn = _device_query) -> "HaloPlan":
+        """The plan from this rank's own [n_local, 4] coordinates (the rank's
+        contiguous range of the grid's (batch, Morton)-sorted rows; every rank
+        holds at least one row).  Collective: every rank of ``group`` calls it."""
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        dev = coords_local.device
+        n = int(coords_local.shape[0])
+        if n == 0:
+            raise ValueError("halo plan: every rank needs at least one row")
+        keys = morton_key(coords_local[:, 0], coords_local[:, 1:])
+        if n > 1 and bool((keys[1:] <= keys[:-1]).any()):
+            raise ValueError("halo plan: rows must be unique and sorted by (batch, Morton code)")
+        meta = torch.tensor([n, int(keys[0]), int(keys[-1])], dtype=torch.int64, device=dev)
+        metas = [torch.empty_like(meta) for _ in range(world)]
+        dist.all_gather(metas, meta, group=group)
+        metas = torch.stack(metas).cpu()
+        counts, firsts, lasts = metas[:, 0], metas[:, 1], metas[:, 2]
+        if world > 1 and bool((firsts[1:] <= lasts[:-1]).any()):
+            raise ValueError("halo plan: ranks' row ranges overlap or are out of order")
+        starts = torch.cumsum(counts, 0) - counts
+        lo = int(starts[rank])
+        splitters = firsts.to(dev)
+
+        # own rows first: a tap that finds no local row may lie in another rank's key range
+        nbr = query_fn(coords_local, coords_local, cfg).to(torch.int32).clone()
+        offs = _kernel_offsets(cfg).to(dev).to(torch.int64)
+        rows, taps = (nbr < 0).nonzero(as_tuple=True)
+        nc = coords_local[rows, 1:].to(torch.int64) + offs[taps]
+        ok = ((nc >= 0) & (nc <= 65534)).all(1)
+        rows, taps, nc = rows[ok], taps[ok], nc[ok]
+        b = coords_local[rows, 0].to(torch.int64)
+        key = morton_key(b, nc)
+        owner = torch.searchsorted(splitters, key, right=True) - 1
+        remote = (owner >= 0) & (owner != rank)
+        rows, taps, nc, b, key = rows[remote], taps[remote], nc[remote], b[remote], key[remote]
+        ukey, inv = torch.unique(key, sorted=True, return_inverse=True)
+        ucoord = torch.empty((ukey.numel(), 4), dtype=torch.int32, device=dev)
+        ucoord[inv] = torch.cat([b[:, None], nc], 1).to(torch.int32)
+        uowner = torch.searchsorted(splitters, ukey, right=True) - 1
+        req_counts = torch.bincount(uowner, minlength=world).to(torch.int64)
+        cnt_in = torch.empty_like(req_counts)
         dist.all_to_all_single(cnt_in, req_counts, group=group)
-        recv_counts = req_counts.tolist()             # rows each owner will send me
-        send_counts = cnt_in.tolist()                 # rows I must send to each rank
-        req_in = torch.empty(int(sum(send_counts)), dtype=torch.int64, device=dev)
-        dist.all_to_all_single(req_in, halo_ids.contiguous(), output_split_sizes=send_counts,
-                               input_split_sizes=recv_counts, group=group)
-        if req_in.numel() and (int(req_in.min()) < lo or int(req_in.max()) >= hi):
-            raise RuntimeError("halo plan: a peer requested rows this rank does not own")
-        return HaloPlan(rank, world, lo, hi, n_halo, local.to(torch.int32).contiguous(), halo_ids,
-                        (req_in - lo).to(torch.int32).contiguous(), send_counts, recv_counts, group)
+        req_l, in_l = req_counts.tolist(), cnt_in.tolist()
+        req_in = torch.empty((int(sum(in_l)), 4), dtype=torch.int32, device=dev)
+        dist.all_to_all_single(req_in, ucoord, output_split_sizes=in_l, input_split_sizes=req_l, group=group)
+        # the owner's answers: its local row of each requested coordinate, or -1
+        if req_in.shape[0]:
+            ans = query_fn(coords_local, req_in, _point_config())[:, 0].to(torch.int64).contiguous()
+        else:
+            ans = torch.empty(0, dtype=torch.int64, device=dev)
+        back = torch.empty(int(sum(req_l)), dtype=torch.int64, device=dev)
+        dist.all_to_all_single(back, ans, output_split_sizes=req_l, input_split_sizes=in_l, group=group)
+        exists = back >= 0
+        n_halo = int(exists.sum())
+        hid = torch.where(exists, n + torch.cumsum(exists.to(torch.int64), 0) - 1, torch.full_like(back, -1))
+        nbr[rows, taps] = hid[inv].to(torch.int32)
+        recv_counts = torch.bincount(uowner[exists], minlength=world).tolist()
+        halo_global = (starts.to(dev)[uowner] + back)[exists]
+        sent = ans >= 0
+        send_local = ans[sent]
+        src_rank = torch.repeat_interleave(torch.arange(world, device=dev), cnt_in)
+        send_counts = torch.bincount(src_rank[sent], minlength=world).tolist()
+
+        # plan order: interior rows first, then the boundary (reads a halo row, or is sent)
+        bnd = (nbr >= n).any(1)
+        if send_local.numel():
+            bnd[send_local] = True
+        order = torch.cat([(~bnd).nonzero()[:, 0], bnd.nonzero()[:, 0]])
+        rank_of = torch.empty(n, dtype=torch.int64, device=dev)
+        rank_of[order] = torch.arange(n, device=dev)
+        nb = nbr[order].to(torch.int64)
+        own = (nb >= 0) & (nb < n)
+        nb = torch.where(own, rank_of[nb.clamp(0, n - 1)], nb)
+        return HaloPlan(rank, world, lo, n, n_halo, int((~bnd).sum()), order.to(torch.int32).contiguous(),
+                        nb.to(torch.int32).contiguous(), halo_global.contiguous(),
+                        rank_of[send_local].to(torch.int32).contiguous(), send_counts, recv_counts, group)
 
     def buffer(self, channels: int, dtype, device) -> torch.Tensor:
-        """A [n_local + n_halo, C] layer buffer: the conv writes rows [0, n_local)."""
+        """A [n_local + n_halo, C] layer buffer in plan order: the convs write rows [0, n_local)."""
         return torch.empty((self.n_local + self.n_halo, channels), dtype=dtype, device=device)
 
     def exchange(self, buf: torch.Tensor, gather_fn: GatherFn = _default_gather) -> torch.Tensor:
@@ -120,30 +221,71 @@ class HaloPlan:
                                input_split_sizes=self.send_counts, group=self.group)
         return buf
 
+    def inverse_order(self) -> torch.Tensor:
+        """[n_local] int32: Morton-local row -> plan row."""
+        inv = torch.empty_like(self.order)
+        inv[self.order.to(torch.int64)] = torch.arange(self.n_local, dtype=torch.int32, device=self.order.device)
+        return inv
+
 
 class ShardedSubmStack:
-    """SubM layer stack on a Morton-range-sharded grid: per layer one halo
-    exchange (pack + all_to_all into the layer buffer), then the local conv
-    over [n_local + n_halo] input rows writing the next buffer's own rows."""
+    """SubM layer stack on a Morton-range-sharded grid.  Per layer: the
+    interior rows' conv on the compute stream while the halo exchange (pack +
+    all-to-all) runs on a second stream, then the boundary rows' conv once the
+    halo has arrived.  Input and output rows are in Morton-local order."""
 
-    def __init__(self, stack, plan: HaloPlan, schedule=None):
+    def __init__(self, stack, plan: HaloPlan, schedule: bool = True, _scheds=None):
+        from . import flex_gmm as F
+
         self.stack = stack      # blocks.SubmStack
         self.plan = plan
-        self.schedule = schedule
+        cfg = stack.cfgs[0]
+        ni = plan.n_interior
+        self.nbr_int = plan.nbr_local[:ni]
+        self.nbr_bnd = plan.nbr_local[ni:]
+        if _scheds is not None:
+            self.sched_int, self.sched_bnd = _scheds
+        else:
+            # conv schedules of the two row sets (tap-mask row order, computed once)
+            self.sched_int = F.neighbor_schedule(cfg, self.nbr_int) if ni and schedule else None
+            self.sched_bnd = F.neighbor_schedule(cfg, self.nbr_bnd) if plan.n_local > ni and schedule else None
         self.bufs = None
+        self.comm = None
+        self._inv = None
+
+    def twin(self) -> "ShardedSubmStack":
+        """A second instance on the same plan and schedules with its own layer
+        buffers (e.g. for a second pipelined input slot)."""
+        return ShardedSubmStack(self.stack, self.plan, _scheds=(self.sched_int, self.sched_bnd))
 
     def forward(self, x_local: torch.Tensor) -> torch.Tensor:
         from . import flex_gmm as F
 
-        plan, n = self.plan, self.plan.n_local
+        plan, n, ni = self.plan, self.plan.n_local, self.plan.n_interior
+        dev = x_local.device
         if self.bufs is None:
-            self.bufs = [plan.buffer(c.in_channels, x_local.dtype, x_local.device) for c in self.stack.cfgs]
-        self.bufs[0][:n].copy_(x_local)
-        out = None
-        for i, (cfg, w, b) in enumerate(zip(self.stack.cfgs, self.stack.w, self.stack.b)):
+            self.bufs = [plan.buffer(c.in_channels, x_local.dtype, dev) for c in self.stack.cfgs]
+            self.out = torch.empty((n, self.stack.cfgs[-1].out_channels), dtype=x_local.dtype, device=dev)
+            self.comm = torch.cuda.Stream(dev)
+            self._inv = plan.inverse_order()
+        compute = torch.cuda.current_stream(dev)
+        F.gather_rows(x_local, plan.order, out=self.bufs[0][:n])
+        layers = list(zip(self.stack.cfgs, self.stack.w, self.stack.b))
+        for i, (cfg, w, b) in enumerate(layers):
             buf = self.bufs[i]
-            plan.exchange(buf)
-            dst = self.bufs[i + 1][:n] if i + 1 < len(self.bufs) else None
-            out = F.sparse_subm_conv_forward(cfg, buf, plan.nbr_local, w, b,
-                                             F.Epilogue(silu=self.stack.silu, schedule=self.schedule), out=dst)
-        return out
+            dst = self.bufs[i + 1][:n] if i + 1 < len(layers) else self.out
+            ready = torch.cuda.Event()
+            ready.record(compute)
+            with torch.cuda.stream(self.comm):
+                self.comm.wait_event(ready)
+                plan.exchange(buf)
+                halo = torch.cuda.Event()
+                halo.record(self.comm)
+            if ni:
+                F.sparse_subm_conv_forward(cfg, buf, self.nbr_int, w, b,
+                                           F.Epilogue(silu=self.stack.silu, schedule=self.sched_int), out=dst[:ni])
+            compute.wait_event(halo)
+            if n > ni:
+                F.sparse_subm_conv_forward(cfg, buf, self.nbr_bnd, w, b,
+                                           F.Epilogue(silu=self.stack.silu, schedule=self.sched_bnd), out=dst[ni:])
+        return F.gather_rows(self.out, self._inv)

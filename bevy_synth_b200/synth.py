@@ -39,10 +39,22 @@ def morton_sort(coords: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(c[order])
 
 
+def _sorted_unique(key: np.ndarray) -> np.ndarray:
+    """Sorted unique values of a 1-D array (sort + adjacent difference: the same
+    result as np.unique, whose hash-based path is ~80x slower on 7M int64 keys)."""
+    s = np.sort(key)
+    if s.size == 0:
+        return s
+    keep = np.empty(s.size, bool)
+    keep[0] = True
+    np.not_equal(s[1:], s[:-1], out=keep[1:])
+    return s[keep]
+
+
 def _unique_xyz(xyz: np.ndarray) -> np.ndarray:
     """Unique rows of non-negative [M,3] int coordinates (< 2^21 each), via 1-D keys."""
     xyz = np.asarray(xyz, np.int64).reshape(-1, 3)
-    key = np.unique((xyz[:, 0] << 42) | (xyz[:, 1] << 21) | xyz[:, 2])
+    key = _sorted_unique((xyz[:, 0] << 42) | (xyz[:, 1] << 21) | xyz[:, 2])
     mask = (1 << 21) - 1
     return np.stack([key >> 42, (key >> 21) & mask, key & mask], axis=1).astype(np.int32)
 
@@ -220,24 +232,31 @@ def child_mask(seed: int, rows: int, p: float = 0.5) -> np.ndarray:
 
 
 def config4(seed: int = 0, assets: int = 64, layers: int = 8, channels: int = 512,
-            asset_ids=None) -> Workload:
+            asset_ids=None, feats: bool = True) -> Workload:
     """64 assets, each a 64^3 sphere shell (radius U(16,28), thickness 2) at
     (32,32,32); batch index in coord[0]; 8 x (SubM 512->512 + SiLU).
-    ``asset_ids`` selects a subset (a rank's shard) with identical content."""
+    ``asset_ids`` selects a subset (a rank's shard) with identical content.
+    With ``feats=False`` no host features are drawn; ``extra["rows"]`` holds
+    each selected asset's row count and ``extra["feat_seeds"]`` its feature
+    seed (for ``device_normal``)."""
     rng = np.random.default_rng(seed)
     radii = rng.uniform(16, 28, assets)
     ws = [normal_weight(rng, channels, channels) for _ in range(layers)]
     bs = [np.zeros(channels, np.float32) for _ in range(layers)]
     ids = range(assets) if asset_ids is None else asset_ids
-    parts, feats = [], []
+    parts, fs, rows, seeds = [], [], [], []
     for b in ids:
         c = morton_sort(unique_cells(b, sphere_shell(64, (32.0, 32.0, 32.0), radii[b], 1.0)))
         parts.append(c)
-        frng = np.random.default_rng(seed * 1000003 + 17 + b)
-        feats.append(frng.standard_normal((c.shape[0], channels)).astype(np.float32))
+        rows.append(c.shape[0])
+        seeds.append(seed * 1000003 + 17 + b)
+        if feats:
+            frng = np.random.default_rng(seeds[-1])
+            fs.append(frng.standard_normal((c.shape[0], channels)).astype(np.float32))
     coords = np.concatenate(parts) if parts else np.zeros((0, 4), np.int32)
-    f = np.concatenate(feats) if feats else np.zeros((0, channels), np.float32)
-    return Workload("cfg4_batched_assets_bf16_512", coords, f, {"w": ws, "b": bs}, {"radii": radii})
+    f = (np.concatenate(fs) if fs else np.zeros((0, channels), np.float32)) if feats else None
+    return Workload("cfg4_batched_assets_bf16_512", coords, f, {"w": ws, "b": bs},
+                    {"radii": radii, "rows": rows, "feat_seeds": seeds})
 
 
 def config5_coords(seed: int = 0, shells: int = 32, grid: int = 1024,
@@ -252,16 +271,39 @@ def config5_coords(seed: int = 0, shells: int = 32, grid: int = 1024,
     return morton_sort(unique_cells(0, np.concatenate(cells)))
 
 
-def config5(seed: int = 0, grid: int = 1024, shells: int = 32) -> Workload:
+CONFIG5_CHANNELS = [(64, 64), (64, 256), (256, 256), (256, 256)]
+
+
+def config5_params(seed: int = 0) -> dict:
+    """The four SubM layers of config 5, weights N(0, 0.02^2), bias 0.  Drawn
+    from their own stream so that they do not depend on the feature draw."""
+    rng = np.random.default_rng(seed + 0x5EED)
+    ws = [normal_weight(rng, co, ci) for ci, co in CONFIG5_CHANNELS]
+    bs = [np.zeros(co, np.float32) for _, co in CONFIG5_CHANNELS]
+    return {"w": ws, "b": bs, "chans": list(CONFIG5_CHANNELS)}
+
+
+def config5(seed: int = 0, grid: int = 1024, shells: int = 32, feats: bool = True) -> Workload:
     """Four SubM layers on the 1024^3 union of shells: two read C=64 features
-    (64->64, 64->256) and two read C=256 (256->256, 256->256)."""
+    (64->64, 64->256) and two read C=256 (256->256, 256->256).  With
+    ``feats=False`` the [N, 64] features are left out (the GPU workloads draw
+    them on the device with ``device_normal``)."""
     rng = np.random.default_rng(seed)
     coords = config5_coords(seed, shells, grid)
-    feats = rng.standard_normal((coords.shape[0], 64)).astype(np.float32)
-    chans = [(64, 64), (64, 256), (256, 256), (256, 256)]
-    ws = [normal_weight(rng, co, ci) for ci, co in chans]
-    bs = [np.zeros(co, np.float32) for _, co in chans]
-    return Workload("cfg5_sharded_grid_bf16", coords, feats, {"w": ws, "b": bs, "chans": chans}, {})
+    f = rng.standard_normal((coords.shape[0], 64)).astype(np.float32) if feats else None
+    return Workload("cfg5_sharded_grid_bf16", coords, f, config5_params(seed), {})
+
+
+def device_normal(seed: int, rows: int, cols: int, device, dtype=None):
+    """Seeded N(0, 1) features drawn on a CUDA device (torch's Philox stream):
+    the large configs' inputs without a host-side draw of billions of values.
+    Deterministic for a given seed, shape and device type."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    x = torch.randn((rows, cols), generator=g, device=device, dtype=torch.float32)
+    return x.to(dtype) if dtype is not None else x
 
 
 def convnext_stage(seed: int = 0, channels: int = 256, hidden: int = 1024, blocks: int = 2) -> Workload:

@@ -46,16 +46,20 @@ def main():
         full_nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct)
         full = stack.forward(x, full_nbr)
         ranges = sharding.morton_ranges(n, world)
-        plan = sharding.HaloPlan.build(ct, ranges, rank,
-                                       lambda a, q: F.neighbor_rows_query_tensor(cfg, a, q))
-        sched = F.neighbor_schedule(cfg, plan.nbr_local)
-        sharded = sharding.ShardedSubmStack(stack, plan, sched)
         lo, hi = ranges[rank]
+        plan = sharding.HaloPlan.build_local(ct[lo:hi].contiguous(), cfg)
+        # the local map, with plan rows and halo rows put back to global ids, is the global map's rows
+        glob_of = torch.cat([lo + plan.order.to(torch.int64), plan.halo_global])
+        nl = plan.nbr_local.to(torch.int64)
+        remapped = torch.where(nl >= 0, glob_of[nl.clamp(min=0)], torch.full_like(nl, -1))
+        maps_equal = bool(torch.equal(remapped.to(torch.int32), full_nbr[lo + plan.order.to(torch.int64)]))
+        sharded = sharding.ShardedSubmStack(stack, plan)
         y = sharded.forward(x[lo:hi].contiguous())
         y2 = sharded.forward(x[lo:hi].contiguous())   # second pass reuses the buffers
         torch.cuda.synchronize()
-        out["morton"] = {"rows": hi - lo, "halo": plan.n_halo, "rel": rel(y, full[lo:hi]),
-                         "repeat_equal": bool(torch.equal(y, y2))}
+        out["morton"] = {"rows": hi - lo, "halo": plan.n_halo, "interior": plan.n_interior,
+                         "rel": rel(y, full[lo:hi]), "repeat_equal": bool(torch.equal(y, y2)),
+                         "maps_equal": maps_equal}
         # --- asset sharding ---------------------------------------------------
         n_assets = 4 * world
         wl_all = synth.config4(seed=2, assets=n_assets, layers=2, channels=128)
@@ -72,7 +76,8 @@ def main():
         sel = torch.as_tensor(np.isin(wl_all.coords[:, 0], mine), device=dev)
         out["assets"] = {"assets": mine, "rows": int(cm.shape[0]), "rel": rel(ym, ya[sel])}
         out["fault"] = _lib.device_fault()
-        ok = (out["morton"]["rel"] <= 1e-6 and out["morton"]["repeat_equal"] and out["assets"]["rel"] <= 1e-6
+        ok = (out["morton"]["rel"] <= 1e-6 and out["morton"]["repeat_equal"] and out["morton"]["maps_equal"]
+              and out["assets"]["rel"] <= 1e-6
               and out["fault"] == 0)
         out["ok"] = ok
     finally:

@@ -1,4 +1,4 @@
-"""Multi-rank logic on CPU (gloo, world sizes 2 and 3): asset shards, Morton
+"""Multi-rank logic on CPU (gloo, world sizes 2, 3 and 4): asset shards, Morton
 ranges, and the halo plan/exchange.  Each rank's conv over its halo-extended
 buffer must equal the global conv's rows exactly (the reference's own chunk
 test shows that a chunk without a halo does not:
@@ -42,9 +42,11 @@ def _grid():
     return coords
 
 
-def _oracle_map(all_c: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
-    cfg = oracle.OracleConfig(1, 1)
-    m = oracle.build_neighbor_rows(cfg, all_c.numpy().astype(np.uint32), oracle.DUP_LOWEST,
+def _oracle_query(table: torch.Tensor, q: torch.Tensor, cfg) -> torch.Tensor:
+    """The map on the CPU oracle (lib.rs:69-109, lowest row on duplicates)."""
+    oc = oracle.OracleConfig(1, 1, cfg.kernel_d, cfg.kernel_h, cfg.kernel_w, axis_order=cfg.axis_order,
+                             axis_sign=cfg.axis_sign)
+    m = oracle.build_neighbor_rows(oc, table.numpy().astype(np.uint32), oracle.DUP_LOWEST,
                                    q.numpy().astype(np.uint32))
     return torch.from_numpy(m)
 
@@ -54,30 +56,43 @@ def _worker(rank, world, port, q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        from bevy_synth_b200 import flex_gmm as F
         coords = torch.from_numpy(_grid())
         n = coords.shape[0]
         ranges = sharding.morton_ranges(n, world)
-        plan = sharding.HaloPlan.build(coords, ranges, rank, _oracle_map)
+        lo, hi = ranges[rank]
+        fcfg = F.SparseSubmConvConfig.subm3(8, 8)
+        plan = sharding.HaloPlan.build_local(coords[lo:hi].contiguous(), fcfg, query_fn=_oracle_query)
+        assert plan.lo == lo and plan.n_local == hi - lo
         rng = np.random.default_rng(1)
         c = 8
         x = rng.standard_normal((n, c)).astype(np.float32)
         w = (rng.standard_normal((c, 3, 3, 3, c)) * 0.1).astype(np.float32)
         b = rng.standard_normal(c).astype(np.float32)
-        lo, hi = ranges[rank]
+        order = plan.order.numpy().astype(np.int64)
         buf = plan.buffer(c, torch.float32, "cpu")
-        buf[:plan.n_local] = torch.from_numpy(x[lo:hi])
+        buf[:plan.n_local] = torch.from_numpy(x[lo:hi][order])
         plan.exchange(buf)
         np.testing.assert_array_equal(buf[plan.n_local:].numpy(), x[plan.halo_global.numpy()])
         cfg = oracle.OracleConfig(c, c)
-        local = oracle.subm_conv_flex(cfg, w, b, buf.numpy(), plan.nbr_local.numpy(), threads=1)
         full_map = oracle.build_neighbor_rows(cfg, coords.numpy().astype(np.uint32))
-        glob = oracle.subm_conv_flex(cfg, w, b, x, full_map, threads=1)[lo:hi]
-        q.put((rank, bool(np.array_equal(local, glob)), plan.n_halo, int(plan.send_idx.numel())))
+        # the local map, with plan rows and halo rows put back to global ids, is the global map's rows
+        glob_of = np.concatenate([lo + order, plan.halo_global.numpy()])
+        nl = plan.nbr_local.numpy()
+        remapped = np.where(nl >= 0, glob_of[np.maximum(nl, 0)], -1)
+        maps_equal = bool(np.array_equal(remapped, full_map[lo + order]))
+        # interior rows read no halo row; boundary rows hold every sent row
+        ni = plan.n_interior
+        interior_ok = bool((nl[:ni] < plan.n_local).all()) and bool((plan.send_idx.numpy() >= ni).all())
+        local = oracle.subm_conv_flex(cfg, w, b, buf.numpy(), nl, threads=1)
+        glob = oracle.subm_conv_flex(cfg, w, b, x, full_map, threads=1)[lo:hi][order]
+        q.put((rank, bool(np.array_equal(local, glob)) and maps_equal and interior_ok, plan.n_halo,
+               int(plan.send_idx.numel())))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_halo_exchange_reproduces_global_conv(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
