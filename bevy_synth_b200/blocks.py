@@ -136,9 +136,12 @@ class C2SUpsampleBlock:
         self.group_children = True
 
     def forward(self, coords: torch.Tensor, x: torch.Tensor, mask: torch.Tensor | None = None, nbr_parent=None,
-                threshold: float = 0.0):
+                threshold: float = 0.0, keep: dict | None = None):
         """Returns (child_coords, child_feats, child_nbr).  Without ``mask`` the
-        children come from the to_subdiv head on x (logits > threshold)."""
+        children come from the to_subdiv head on x (logits > threshold).  With
+        ``keep`` (a dict) the intermediates are left in it: ``h`` (parents after
+        LN + SiLU), ``h_up`` (children after conv1's LN + SiLU epilogue),
+        ``child_row`` ([Np, 8] child of each parent block), ``nbr_parent``."""
         p = self.p
         if mask is None:
             if p.w_sub is None:
@@ -163,6 +166,8 @@ class C2SUpsampleBlock:
         y = F.sparse_subm_conv_forward(
             self.cfg2, h_up, nbr_child, p.w2, p.b2,
             F.Epilogue(residual=x, residual_offset=skip_off, residual_repeat=rep))
+        if keep is not None:
+            keep.update(h=h, h_up=h_up, child_row=child_row, nbr_parent=nbr_parent)
         return child_coords, y, nbr_child
 
     def flops(self, nbr_parent: torch.Tensor, nbr_child: torch.Tensor, mask: torch.Tensor) -> float:

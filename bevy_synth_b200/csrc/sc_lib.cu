@@ -474,21 +474,15 @@ constexpr int64_t kStaticMaxRows = kStaticTableSlots / 2;        // 262,144 inpu
 constexpr size_t kStaticScratchBytes = 256 + (size_t)kStaticTableSlots * sizeof(HashSlot);
 static __device__ __align__(256) uint8_t g_nb_static_scratch[kStaticScratchBytes];
 
-// Device address of g_nb_static_scratch, resolved once per device with that
-// device current (in host code the symbol itself is only a host-side stand-in).
+// Device address of g_nb_static_scratch on the calling thread's current device
+// (in host code the symbol itself is only a host-side stand-in).  Resolved on
+// every call rather than cached: the lookup is cheap, and a cached address
+// would dangle once the device's primary context is reset and the module
+// reloaded.
 static int static_scratch_address(void** out) {
-    static std::mutex mu;
-    static void* addr[128] = {nullptr};
-    int dev = 0;
-    SC_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 128) return fail(SC_ERR_UNSUPPORTED, "device index out of range");
-    std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
-        void* p = nullptr;
-        SC_CUDA_TRY(cudaGetSymbolAddress(&p, g_nb_static_scratch));
-        addr[dev] = p;
-    }
-    *out = addr[dev];
+    void* p = nullptr;
+    SC_CUDA_TRY(cudaGetSymbolAddress(&p, g_nb_static_scratch));
+    *out = p;
     return SC_OK;
 }
 

@@ -115,7 +115,7 @@ class Cfg5(_Base):
             self.lo, self.hi = 0, n
 
             def setup():
-                holder["nbr"] = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct, check_status=False)
+                holder["nbr"] = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct)
                 holder["sched"] = F.neighbor_schedule(cfg, holder["nbr"])
 
             self.setup_ms = _events_ms(setup, dev)
@@ -203,7 +203,7 @@ class Cfg4(_Base):
         holder = {}
 
         def setup():
-            holder["nbr"] = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct, check_status=False)
+            holder["nbr"] = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct)
             holder["sched"] = F.neighbor_schedule(cfg, holder["nbr"])
 
         self.setup_ms = _events_ms(setup, dev)
@@ -253,7 +253,7 @@ class Cfg2(_Base):
         holder = {}
 
         def setup():
-            holder["nbr"] = F.neighbor_rows_tensor_from_coords_tensor(self.stack.cfg, ct, check_status=False)
+            holder["nbr"] = F.neighbor_rows_tensor_from_coords_tensor(self.stack.cfg, ct)
             holder["sched"] = F.neighbor_schedule(self.stack.cfg, holder["nbr"])
 
         self.setup_ms = _events_ms(setup, dev)

@@ -140,8 +140,8 @@ int sc_neighbor_status(const void* d_workspace, int32_t* h_max_probe, void* stre
  *  - The hash table lives in a fixed 8 MiB static device array that every GPU
  *    loading the library holds until exit; n_rows is limited to 262,144
  *    (SC_ERR_CAPACITY beyond, checked before any GPU work).
- *  - The first call on a device resolves the array's device address with
- *    that device current; make that first call before any stream capture.
+ *  - Every call looks up the array's device address on the calling thread's
+ *    current device (cudaGetSymbolAddress; no allocation).
  *  - Every call shares the one array and clears it first: calls that overlap
  *    on the GPU (other streams, other host threads) race and must be
  *    serialised by the caller.
@@ -174,13 +174,21 @@ int sc_neighbor_schedule_grouped(const sc_conv_config* cfg, const int32_t* d_nei
 
 /* ---- convolution ----------------------------------------------------------
  * out[n_rows, Cout] = bias + sum_k sum_c in[nbr[r,k], c] * W[o,k,c]  (+ epilogue)
- * d_input [n_in, Cin], d_neighbor_rows [n_rows, K] (n_rows <= n_in is not
- * required: query maps may address any input row < n_in), d_weight
- * [Cout, KD, KH, KW, Cin/groups] in `dtype`, d_bias [Cout] fp32 (nullable =
- * zero).  fp32 accumulates in fp32 FFMA; bf16 runs on tcgen05 tensor cores
- * (fp32 accumulation in TMEM) when groups == 1, Cin % 8 == 0, Cout % 16 == 0
- * and K <= 32, otherwise on a CUDA-core kernel.  Neighbor indices outside
- * [-1, n_in) read as zero and raise the device fault word. */
+ * d_input [n_in, Cin], d_neighbor_rows [n_rows, K] with n_rows <= n_in
+ * (SC_ERR_INVALID otherwise, as the reference's "neighbor row count exceeds
+ * input rows" check, src/wgpu/sparse_conv.rs:439-444; the map's entries may
+ * address any input row < n_in, e.g. halo rows appended after the query
+ * rows), d_weight [Cout, KD, KH, KW, Cin/groups] in `dtype`, d_bias [Cout]
+ * fp32 (nullable = zero).  fp32 accumulates in fp32 FFMA.  bf16 runs on
+ * tcgen05 tensor cores (fp32 accumulation in TMEM) when groups == 1, K <= 32,
+ * Cin >= 64, Cin % 8 == 0, Cout % 32 == 0, the output column tile (Cout, or
+ * Cout / out_row_map_cols with a row map) is at most 512 wide with any
+ * LayerNorm width dividing it, and every pointer the kernel reads in 16-byte
+ * vectors (input, weight, bias, map, residual, LayerNorm parameters, outputs)
+ * is 16-byte aligned; otherwise on a CUDA-core kernel
+ * (sc_conv_uses_tensor_cores reports the choice for an unfused conv).
+ * Neighbor indices outside [-1, n_in) read as zero and raise the device fault
+ * word. */
 int sc_subm_conv_forward(const sc_conv_config* cfg, sc_dtype dtype, const void* d_input,
                          int64_t n_in, const int32_t* d_neighbor_rows, int64_t n_rows,
                          const void* d_weight, const float* d_bias, const sc_epilogue* epi,
