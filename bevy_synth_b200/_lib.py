@@ -31,7 +31,7 @@ EXPORTED = (
     "sc_subm_conv_forward", "sc_conv_uses_tensor_cores", "sc_layer_norm_act", "sc_bf16_round",
     "sc_cast", "sc_subdivide_scratch_bytes", "sc_subdivide", "sc_gather_rows", "sc_subdiv_head",
     "sc_patchify3d_scratch_bytes", "sc_patchify3d_forward", "sc_neighbor_schedule_grouped_scratch_bytes",
-    "sc_neighbor_schedule_grouped",
+    "sc_neighbor_schedule_grouped", "sc_set_wait_limit_ns",
 )
 
 
@@ -85,6 +85,7 @@ _SIGS = {
     "sc_version": ([], ctypes.c_int),
     "sc_last_error": ([ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
     "sc_device_fault": ([ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+    "sc_set_wait_limit_ns": ([ctypes.c_uint64], ctypes.c_int),
     "sc_kernel_rows": ([_P, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "sc_kernel_offsets": ([_P, _P], ctypes.c_int),
     "sc_neighbor_workspace_bytes": ([_I64, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
@@ -138,6 +139,16 @@ def last_error() -> str:
 def check(rc: int) -> None:
     if rc != SC_OK:
         raise SparseConvError(rc, last_error())
+
+
+FAULT_WAIT_TIMEOUT = 1 << 0
+FAULT_BAD_NEIGHBOR = 1 << 1
+FAULT_TMEM = 1 << 2
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Time limit of the kernels' bounded waits on the current device (0 = the 2 s default)."""
+    check(lib().sc_set_wait_limit_ns(int(ns)))
 
 
 def device_fault() -> int:

@@ -106,6 +106,7 @@ struct TcParams {
     int map_cols;
     const int32_t* row_order;    // nullable: tile position -> output row (a permutation)
     const int32_t* nbr_ordered;  // nullable: nbr rows in tile order (nbr[row_order[p]])
+    int test_stall;              // test only (single CTA): the MMA warp waits on a barrier nothing completes
 };
 
 // Output row processed at tile position `pos` (< n_rows), or -1 if invalid.
@@ -294,7 +295,8 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
     uint64_t* sched_full = bars + 3 * S + 4;               // [TC_SCHED] response landed
     uint64_t* sched_empty = sched_full + TC_SCHED;         // [TC_SCHED] every role has read it
     uint64_t* mask_bar = sched_empty + TC_SCHED;           // every producer warp posted its tap mask
-    uint64_t* pair_bar = mask_bar + 1;                     // PAIR: the peer CTA's tap mask arrived
+    uint64_t* pair_bar = mask_bar + 1;                     // PAIR: the peer CTA's tap mask arrived (single CTA:
+                                                           // never arrived; the test stall mode waits on it)
     uint64_t* res_bar = pair_bar + 1;                      // [4] per epilogue warp: staged residual rows landed
     uint32_t* stage_flags = reinterpret_cast<uint32_t*>(res_bar + 4);  // [S] 2 = a tile's last step (bookkeeping, not read)
     uint32_t* tile_steps = stage_flags + S;  // [8] reduction steps per tile, ring over tiles
@@ -753,7 +755,7 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
                             break;
                         }
                         if (it >= *total) break;
-                        if ((spin & 255u) == 255u && globaltimer() - t0 > kWaitLimitNs) {
+                        if ((spin & 255u) == 255u && globaltimer() - t0 > wait_limit_ns()) {
                             raise_fault(FAULT_WAIT_TIMEOUT);
                             *abort_flag = 1u;
                             break;
@@ -783,6 +785,12 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
             for (int64_t lt = 0; tile >= 0 && ok; ++lt) {
                 const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
                 const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
+                // Test mode: a wait that nothing completes, so that every role reaches its wait
+                // limit, raises FAULT_WAIT_TIMEOUT and drains (no stage is consumed, no MMA issued).
+                if (!PAIR && p.test_stall && !__all_sync(0xffffffffu, mbar_wait(pair_bar, 0u))) {
+                    ok = false;
+                    break;
+                }
                 if (!__all_sync(0xffffffffu, mbar_wait(&tmem_empty[b], (use & 1u) ^ 1u))) {
                     ok = false;
                     break;

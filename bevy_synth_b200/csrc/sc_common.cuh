@@ -42,8 +42,15 @@ __device__ uint32_t g_fault;
 
 __device__ __forceinline__ void raise_fault(uint32_t bits) { atomicOr(&g_fault, bits); }
 
-// Time limit of every spin-wait in device code (ns of %globaltimer).
+// Default time limit of every spin-wait in device code (ns of %globaltimer).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// The limit in force on this device (sc_set_wait_limit_ns changes it; every
+// bounded wait reads it when it checks the timer).
+__device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
+
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+    return *reinterpret_cast<volatile const uint64_t*>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
@@ -123,13 +130,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and raises FAULT_WAIT_TIMEOUT) if the phase
-// with `parity` has not completed within kWaitLimitNs.
+// with `parity` has not completed within the wait limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer();
     for (uint32_t spin = 1;; ++spin) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((spin & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+        if ((spin & 255u) == 0 && globaltimer() - t0 > wait_limit_ns()) {
             raise_fault(FAULT_WAIT_TIMEOUT);
             return false;
         }
@@ -277,7 +284,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
             : "r"(smem_u32(bar)), "r"(parity)
             : "memory");
         if (ok) return true;
-        if ((spin & 255u) == 255u && globaltimer() - t0 > kWaitLimitNs) {
+        if ((spin & 255u) == 255u && globaltimer() - t0 > wait_limit_ns()) {
             raise_fault(FAULT_WAIT_TIMEOUT);
             return false;
         }

@@ -335,6 +335,12 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     p.map_cols = e.d_out_row_map ? e.out_row_map_cols : 1;
     p.row_order = e.d_row_order;
     p.nbr_ordered = e.d_row_order ? e.d_neighbor_rows_ordered : nullptr;
+    {
+        // SC_TC_TEST_STALL=1 (tests only, read on every call): the single-CTA kernel's MMA warp waits
+        // on a barrier that nothing completes, to drive the bounded waits to their limit
+        const char* st_env = std::getenv("SC_TC_TEST_STALL");
+        p.test_stall = (st_env && st_env[0] == '1' && !plan.pair) ? 1 : 0;
+    }
 
     static std::once_flag attr_once;
     static cudaError_t attr_err = cudaSuccess;
@@ -510,6 +516,12 @@ int sc_device_fault(uint32_t* h_fault) {
     SC_CUDA_TRY(cudaMemcpyFromSymbol(h_fault, g_fault, sizeof(uint32_t)));
     const uint32_t zero = 0;
     SC_CUDA_TRY(cudaMemcpyToSymbol(g_fault, &zero, sizeof(uint32_t)));
+    return SC_OK;
+}
+
+int sc_set_wait_limit_ns(uint64_t ns) {
+    const uint64_t v = ns ? ns : kWaitLimitNs;
+    SC_CUDA_TRY(cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof v));
     return SC_OK;
 }
 

@@ -539,3 +539,47 @@ def sparse_patchify3d_forward(config: SparsePatchify3dConfig, input: torch.Tenso
                                       _ptr(coords.contiguous()), rows, _ptr(weight.contiguous()), _ptr(bias),
                                       _ptr(scratch), int(nbytes.value), _ptr(out), _stream(input)))
     return out
+
+
+def downsample_coords(coords: torch.Tensor) -> torch.Tensor:
+    """Output grid of a stride-2 sparse conv: the distinct cells
+    ``(batch, x >> 1, y >> 1, z >> 1)`` of ``coords``, sorted by (batch, Morton
+    code) like every grid of this path."""
+    from .sharding import morton_key
+
+    _coords_tensor(coords)
+    if coords.shape[0] == 0:
+        return coords.clone()
+    half = torch.cat([coords[:, :1], coords[:, 1:] >> 1], 1)
+    key = morton_key(half[:, 0], half[:, 1:])
+    ukey, inv = torch.unique(key, sorted=True, return_inverse=True)
+    out = torch.empty((ukey.numel(), 4), dtype=torch.int32, device=coords.device)
+    out[inv] = half
+    return out
+
+
+def sparse_conv3d_stride2_forward(input: torch.Tensor, coords: torch.Tensor, weight: torch.Tensor,
+                                  bias: torch.Tensor | None = None, epilogue: Epilogue | None = None,
+                                  out_coords: torch.Tensor | None = None):
+    """Stride-2 sparse downsample convolution (SparseConv3d, kernel 2, stride 2,
+    no padding): the output grid is ``downsample_coords(coords)`` and
+    ``out[o] = bias + sum_{(a,b,c) in {0,1}^3} in[row of 2*o + (a,b,c)] @ W[:, a, b, c, :]^T``
+    (absent input cells contribute nothing).  ``weight`` is [Cout, 2, 2, 2, Cin].
+    The reference has no downsample conv; this is the operation's definition.
+    The 2x2x2 map is a neighbor query of 2*o + 1 (the offsets of a 2-wide kernel
+    are -1 and 0) and the conv runs on the same gather-GEMM kernels as SubM.
+    Returns (out_coords [M, 4], out [M, Cout])."""
+    _coords_tensor(coords)
+    if weight.dim() != 5 or tuple(weight.shape[1:4]) != (2, 2, 2):
+        raise SparseConvError(_lib.SC_ERR_INVALID,
+                              f"stride-2 sparse conv weight must be [Cout, 2, 2, 2, Cin], got {list(weight.shape)}")
+    cout, cin = int(weight.shape[0]), int(weight.shape[4])
+    cfg = SparseSubmConvConfig(cin, cout, 2, 2, 2)
+    oc = downsample_coords(coords) if out_coords is None else out_coords
+    query = torch.cat([oc[:, :1], oc[:, 1:] * 2 + 1], 1).contiguous()
+    nbr = neighbor_rows_query_tensor(cfg, coords, query)
+    e = epilogue or Epilogue()
+    if e.schedule is None and e.row_order is None and oc.shape[0]:
+        e.schedule = neighbor_schedule(cfg, nbr)
+    out = sparse_subm_conv_forward(cfg, input, nbr, weight, bias, e)
+    return oc, out

@@ -36,6 +36,7 @@ import torch
 
 from . import blocks, sharding, synth
 from . import flex_gmm as F
+from .sparse_tensor import SparseTensor
 
 BF16 = torch.bfloat16
 
@@ -200,17 +201,14 @@ class Cfg4(_Base):
         _broadcast(self.stack.w + self.stack.b, world, group)
         ct = torch.as_tensor(wl.coords, device=dev)
         cfg = self.stack.cfgs[0]
-        holder = {}
-
-        def setup():
-            holder["nbr"] = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct)
-            holder["sched"] = F.neighbor_schedule(cfg, holder["nbr"])
-
-        self.setup_ms = _events_ms(setup, dev)
-        self.nbr, self.sched = holder["nbr"], holder["sched"]
         parts = [synth.device_normal(s, r, channels, dev, BF16) for s, r in
                  zip(wl.extra["feat_seeds"], wl.extra["rows"])]
         x = torch.cat(parts) if parts else torch.empty((0, channels), dtype=BF16, device=dev)
+        # the rank's assets as one batch-grouped sparse tensor (batch index = asset id)
+        self.sparse = SparseTensor.new(ct, x, 64)
+        assert self.sparse.layout.batch_size() == len(self.assets)
+        self.setup_ms = _events_ms(lambda: self.sparse.neighbor_rows(cfg), dev)
+        self.nbr, self.sched = self.sparse.neighbor_rows(cfg)
         self._x = _Slots(lambda k: x if k == 0 else x.clone())
         self.n_local = int(ct.shape[0])
         self.valid_pairs = _pairs(self.nbr)

@@ -107,6 +107,11 @@ int sc_last_error(char* h_buf, size_t len);
 /* Reads and clears the sticky device fault word of the current device
  * (synchronises the device).  0 = no fault. */
 int sc_device_fault(uint32_t* h_fault);
+/* Sets the time limit of every bounded wait in this library's kernels on the
+ * current device (ns; 0 restores the default of 2 s).  A wait that reaches it
+ * raises FAULT_WAIT_TIMEOUT (bit 0 of the fault word) and its kernel drains
+ * and returns.  No counterpart in the reference (its kernels do not wait). */
+int sc_set_wait_limit_ns(uint64_t ns);
 
 /* ---- kernel layout ------------------------------------------------------- */
 int sc_kernel_rows(const sc_conv_config* cfg, int64_t* h_rows);
