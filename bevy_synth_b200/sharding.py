@@ -241,8 +241,10 @@ class ShardedSubmStack:
         self.plan = plan
         cfg = stack.cfgs[0]
         ni = plan.n_interior
-        self.nbr_int = plan.nbr_local[:ni]
-        self.nbr_bnd = plan.nbr_local[ni:]
+        # separate allocations: a row slice of the [n, 27] map starts 108 * ni bytes in, which is not
+        # 16-byte aligned in general, and the tensor-core kernel reads the map in 16-byte vectors
+        self.nbr_int = plan.nbr_local[:ni].clone()
+        self.nbr_bnd = plan.nbr_local[ni:].clone()
         if _scheds is not None:
             self.sched_int, self.sched_bnd = _scheds
         else:
