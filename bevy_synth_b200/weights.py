@@ -64,6 +64,18 @@ def read_safetensors(path_or_bytes) -> dict:
     return out
 
 
+def read_weights(path: str) -> dict:
+    """name -> TensorView of a decoder weight file: safetensors, or a ``.bpk``
+    blob burnpack (or its ``.parts.json`` split) whose payload is the
+    safetensors file, as the reference's loader accepts
+    (sparse_decoder_loading.rs:315-348)."""
+    if str(path).lower().endswith(".bpk"):
+        from .burnpack import read_blob
+
+        return read_safetensors(read_blob(str(path)))
+    return read_safetensors(path)
+
+
 def write_safetensors(path, tensors: dict, bf16: tuple = ()) -> None:
     """Writes float32 / float16 arrays; names in ``bf16`` are stored as BF16
     (round-to-nearest-even of the float32 values)."""
