@@ -266,6 +266,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cfg5-shells", type=int, default=32,
+                    help="shells of the config-5 grid (32 = BASELINE; fewer give a smaller case for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -290,7 +292,8 @@ def main():
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    wl = WORKLOADS[args.workload](dev, rank, world)
+    kw = {"shells": args.cfg5_shells} if args.workload == "cfg5" else {}
+    wl = WORKLOADS[args.workload](dev, rank, world, **kw)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
 

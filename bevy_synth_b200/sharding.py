@@ -251,9 +251,11 @@ class ShardedSubmStack:
             # conv schedules of the two row sets (tap-mask row order, computed once)
             self.sched_int = F.neighbor_schedule(cfg, self.nbr_int) if ni and schedule else None
             self.sched_bnd = F.neighbor_schedule(cfg, self.nbr_bnd) if plan.n_local > ni and schedule else None
+        # the last layer writes Morton-local rows directly (epilogue row map: plan row p -> order[p])
+        self.order_int = plan.order[:ni].clone()
+        self.order_bnd = plan.order[ni:].clone()
         self.bufs = None
         self.comm = None
-        self._inv = None
 
     def twin(self) -> "ShardedSubmStack":
         """A second instance on the same plan and schedules with its own layer
@@ -261,6 +263,8 @@ class ShardedSubmStack:
         return ShardedSubmStack(self.stack, self.plan, _scheds=(self.sched_int, self.sched_bnd))
 
     def forward(self, x_local: torch.Tensor) -> torch.Tensor:
+        """One pass; returns this instance's [n_local, Cout] output buffer (Morton-local rows),
+        which the next call on the same instance overwrites."""
         from . import flex_gmm as F
 
         plan, n, ni = self.plan, self.plan.n_local, self.plan.n_interior
@@ -269,13 +273,13 @@ class ShardedSubmStack:
             self.bufs = [plan.buffer(c.in_channels, x_local.dtype, dev) for c in self.stack.cfgs]
             self.out = torch.empty((n, self.stack.cfgs[-1].out_channels), dtype=x_local.dtype, device=dev)
             self.comm = torch.cuda.Stream(dev)
-            self._inv = plan.inverse_order()
         compute = torch.cuda.current_stream(dev)
         F.gather_rows(x_local, plan.order, out=self.bufs[0][:n])
         layers = list(zip(self.stack.cfgs, self.stack.w, self.stack.b))
         for i, (cfg, w, b) in enumerate(layers):
             buf = self.bufs[i]
-            dst = self.bufs[i + 1][:n] if i + 1 < len(layers) else self.out
+            last = i + 1 == len(layers)
+            dst = self.out if last else self.bufs[i + 1][:n]
             ready = torch.cuda.Event()
             ready.record(compute)
             with torch.cuda.stream(self.comm):
@@ -283,11 +287,17 @@ class ShardedSubmStack:
                 plan.exchange(buf)
                 halo = torch.cuda.Event()
                 halo.record(self.comm)
-            if ni:
-                F.sparse_subm_conv_forward(cfg, buf, self.nbr_int, w, b,
-                                           F.Epilogue(silu=self.stack.silu, schedule=self.sched_int), out=dst[:ni])
-            compute.wait_event(halo)
-            if n > ni:
-                F.sparse_subm_conv_forward(cfg, buf, self.nbr_bnd, w, b,
-                                           F.Epilogue(silu=self.stack.silu, schedule=self.sched_bnd), out=dst[ni:])
-        return F.gather_rows(self.out, self._inv)
+            for rows, nbr, sched, order, wait in ((slice(0, ni), self.nbr_int, self.sched_int, self.order_int, False),
+                                                  (slice(ni, n), self.nbr_bnd, self.sched_bnd, self.order_bnd, True)):
+                if wait:
+                    compute.wait_event(halo)
+                if rows.stop <= rows.start:
+                    continue
+                if last:  # rows go straight to their Morton-local place
+                    F.sparse_subm_conv_forward(cfg, buf, nbr, w, b, F.Epilogue(
+                        silu=self.stack.silu, schedule=sched, out_row_map=order, out_row_map_cols=1),
+                        out=dst, out_rows=n)
+                else:
+                    F.sparse_subm_conv_forward(cfg, buf, nbr, w, b,
+                                               F.Epilogue(silu=self.stack.silu, schedule=sched), out=dst[rows])
+        return self.out

@@ -99,9 +99,10 @@ class Cfg5(_Base):
     name = "cfg5_sharded_grid_bf16"
     dtype = "bf16"
 
-    def __init__(self, dev, rank: int = 0, world: int = 1, group=None, seed: int = 0, coords=None):
+    def __init__(self, dev, rank: int = 0, world: int = 1, group=None, seed: int = 0, coords=None, shells: int = 32):
         self.dev, self.rank, self.world = dev, rank, world
-        coords_np = synth.config5_coords(seed) if coords is None else coords
+        self.shells = shells
+        coords_np = synth.config5_coords(seed, shells=shells) if coords is None else coords
         self.coords_np = coords_np
         self.params = synth.config5_params(seed)
         self.stack = blocks.SubmStack(self.params["w"], self.params["b"], False, dev)
@@ -163,7 +164,7 @@ class Cfg5(_Base):
     def describe(self) -> dict:
         d = {"workload": self.name, "voxels_total": int(self.n_total), "voxels_this_rank": int(self.n_local),
              "layers": self.launch_labels, "valid_pairs_P_this_rank": int(self.valid_pairs),
-             "grid": "1024^3, union of 32 ellipsoid shells (seed 0)",
+             "grid": f"1024^3, union of {self.shells} ellipsoid shells (seed 0)",
              "step": "4 SubM conv layers (tcgen05, bf16); neighbor map + conv schedule built once per grid",
              "setup_ms": round(self.setup_ms, 3)}
         if self.plan is not None:

@@ -54,7 +54,7 @@ def main():
         remapped = torch.where(nl >= 0, glob_of[nl.clamp(min=0)], torch.full_like(nl, -1))
         maps_equal = bool(torch.equal(remapped.to(torch.int32), full_nbr[lo + plan.order.to(torch.int64)]))
         sharded = sharding.ShardedSubmStack(stack, plan)
-        y = sharded.forward(x[lo:hi].contiguous())
+        y = sharded.forward(x[lo:hi].contiguous()).clone()
         y2 = sharded.forward(x[lo:hi].contiguous())   # second pass reuses the buffers
         torch.cuda.synchronize()
         out["morton"] = {"rows": hi - lo, "halo": plan.n_halo, "interior": plan.n_interior,
