@@ -31,7 +31,8 @@ EXPORTED = (
     "sc_subm_conv_forward", "sc_conv_uses_tensor_cores", "sc_layer_norm_act", "sc_bf16_round",
     "sc_cast", "sc_subdivide_scratch_bytes", "sc_subdivide", "sc_gather_rows", "sc_subdiv_head",
     "sc_patchify3d_scratch_bytes", "sc_patchify3d_forward", "sc_neighbor_schedule_grouped_scratch_bytes",
-    "sc_neighbor_schedule_grouped", "sc_set_wait_limit_ns",
+    "sc_neighbor_schedule_grouped", "sc_set_wait_limit_ns", "sc_neighbor_tile_sources_bytes",
+    "sc_neighbor_tile_sources",
 )
 
 
@@ -74,6 +75,8 @@ class ScEpilogue(ctypes.Structure):
         ("out_row_map_cols", ctypes.c_int32),
         ("d_row_order", ctypes.c_void_p),
         ("d_neighbor_rows_ordered", ctypes.c_void_p),
+        ("d_tile_sources", ctypes.c_void_p),
+        ("tile_sources_max", ctypes.c_int32),
     ]
 
 
@@ -86,6 +89,9 @@ _SIGS = {
     "sc_last_error": ([ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
     "sc_device_fault": ([ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
     "sc_set_wait_limit_ns": ([ctypes.c_uint64], ctypes.c_int),
+    "sc_neighbor_tile_sources_bytes": ([_I64, _I64, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "sc_neighbor_tile_sources": ([_P, _P, _I64, _I64, _P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int32), _P],
+                                 ctypes.c_int),
     "sc_kernel_rows": ([_P, ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "sc_kernel_offsets": ([_P, _P], ctypes.c_int),
     "sc_neighbor_workspace_bytes": ([_I64, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),

@@ -199,6 +199,15 @@ class UpsamplePyramid:
         return coords, x, stats
 
 
+def layer_epilogue(cfg, silu: bool, schedule=None, tile_sources=None) -> F.Epilogue:
+    """Bias [+ SiLU] epilogue of a plain SubM layer: a 64-input-channel layer runs
+    in map order on the map's tile-source plan when one is given, every other
+    layer on the map's conv schedule."""
+    if tile_sources is not None and cfg.in_channels == 64:
+        return F.Epilogue(silu=silu, tile_sources=tile_sources)
+    return F.Epilogue(silu=silu, schedule=schedule)
+
+
 class SubmStack:
     """A chain of SubM3x3x3 layers with an optional SiLU after each (BASELINE
     config 4: 8 x (SubM 512->512 + SiLU); config 5: 64->64, 64->256,
@@ -213,9 +222,11 @@ class SubmStack:
     def conv_count(self) -> int:
         return len(self.w)
 
-    def forward(self, x: torch.Tensor, nbr: torch.Tensor, schedule=None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, nbr: torch.Tensor, schedule=None, tile_sources=None) -> torch.Tensor:
+        """``schedule``: the map's conv schedule (F.neighbor_schedule); ``tile_sources``: its
+        tile-source plan (F.neighbor_tile_sources), taken by the layers with 64 input channels."""
         for cfg, w, b in zip(self.cfgs, self.w, self.b):
-            x = F.sparse_subm_conv_forward(cfg, x, nbr, w, b, F.Epilogue(silu=self.silu, schedule=schedule))
+            x = F.sparse_subm_conv_forward(cfg, x, nbr, w, b, layer_epilogue(cfg, self.silu, schedule, tile_sources))
         return x
 
     def flops(self, nbr: torch.Tensor) -> float:

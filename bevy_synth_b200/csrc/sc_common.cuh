@@ -409,6 +409,19 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (bf16, fp32 accumulate), A read
+// from tensor memory: lane m holds row m, K elements packed two per 32-bit
+// column (element 2c in the low half of column c), so one K=16 step spans 8 columns.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive (once) on `bar` when all previously issued tcgen05.mma complete.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile(

@@ -18,6 +18,7 @@
 
 #include "conv_simt.cuh"
 #include "conv_tc.cuh"
+#include "conv_ts.cuh"
 #include "neighbor.cuh"
 #include "rowops.cuh"
 #include "sc_common.cuh"
@@ -403,6 +404,88 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     return SC_OK;
 }
 
+// The tile-source (A-from-TMEM) kernel: bf16, 64 input channels, <= 256 outputs, a plain bias/SiLU
+// epilogue, map rows in order, and a usable tile-source plan.  SC_TS=0 turns it off.
+struct TsPlan {
+    int tile_n, grid_y, u_cap, stages, stg_cols;
+    size_t smem;
+};
+
+static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, TsPlan* plan) {
+    if (dt != SC_DTYPE_BF16 || c->groups != 1 || force_simt() || !e.d_tile_sources) return false;
+    if (const char* env = std::getenv("SC_TS"))
+        if (env[0] == '0') return false;
+    const int64_t K = kernel_rows_of(c), cin = c->in_channels, cout = c->out_channels;
+    if (cin != 64 || K > 32 || cout % 32 != 0 || cout > 256) return false;
+    if (e.layer_norm || e.d_residual || e.d_out2 || e.d_out_row_map || e.d_row_order) return false;
+    if (e.tile_sources_max < 0 || e.tile_sources_max > TS_UMAX) return false;
+    int tile_n = (int)cout;
+    if (cout > 128) {
+        if (cout % 64 != 0) return false;
+        tile_n = (int)(cout / 2);
+    }
+    plan->tile_n = tile_n;
+    plan->grid_y = (int)(cout / tile_n);
+    plan->u_cap = std::max(8, (e.tile_sources_max + 7) / 8 * 8);
+    plan->stg_cols = tc_stg_cols(tile_n, 64);
+    int S = 8;
+    while (S >= 2 && ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, plan->stg_cols) > kMaxDynSmem) --S;
+    if (S < 2) return false;
+    plan->stages = S;
+    plan->smem = ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, plan->stg_cols);
+    return true;
+}
+
+static int launch_ts(const sc_conv_config* c, const void* in, int64_t n_in, int64_t n_rows, const void* w,
+                     const float* bias, const sc_epilogue& e, void* out, cudaStream_t st, const TsPlan& plan) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const int64_t K = kernel_rows_of(c), cout = c->out_channels;
+    CUtensorMap wmap;
+    cuuint64_t dims[3] = {64u, (cuuint64_t)K, (cuuint64_t)cout};
+    cuuint64_t strides[2] = {64u * 2u, (cuuint64_t)(K * 64 * 2)};
+    cuuint32_t box[3] = {64u, 1u, (cuuint32_t)plan.tile_n};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    CUresult r = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(w), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+    const int64_t row_tiles = (n_rows + 127) / 128;
+    TsPlanView v = ts_plan_view(const_cast<void*>(e.d_tile_sources), row_tiles);
+    TsParams p;
+    memset(&p, 0, sizeof p);
+    p.in = static_cast<const __nv_bfloat16*>(in);
+    p.n_in = n_in;
+    p.n_rows = n_rows;
+    p.K = (int)K;
+    p.u_count = v.u_count;
+    p.tap_mask = v.tap_mask;
+    p.u_rows = v.u_rows;
+    p.lidx = v.lidx;
+    p.bias = bias;
+    p.silu = e.silu;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.cout = (int)cout;
+    p.tile_n = plan.tile_n;
+    p.grid_y = plan.grid_y;
+    p.n_tiles = row_tiles * plan.grid_y;
+    p.u_cap = plan.u_cap;
+    p.b_stages = plan.stages;
+    p.stg_cols = plan.stg_cols;
+    static std::once_flag ts_once;
+    static cudaError_t ts_err = cudaSuccess;
+    std::call_once(ts_once, [] {
+        ts_err = cudaFuncSetAttribute((const void*)conv_ts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kMaxDynSmem);
+    });
+    SC_CUDA_TRY(ts_err);
+    const int64_t ctas = std::min<int64_t>(p.n_tiles, sm_count());
+    conv_ts_kernel<<<(unsigned)ctas, TS_THREADS, plan.smem, st>>>(wmap, p);
+    SC_CUDA_TRY(cudaGetLastError());
+    return SC_OK;
+}
+
 template <typename T>
 static int launch_simt(const sc_conv_config* c, const void* in, int64_t n_in, const int32_t* nbr,
                        int64_t n_rows, const void* w, const float* bias, const sc_epilogue& e,
@@ -677,6 +760,41 @@ int sc_neighbor_schedule(const sc_conv_config* cfg, const int32_t* nbr, int64_t 
     return SC_OK;
 }
 
+int sc_neighbor_tile_sources_bytes(int64_t n_rows, int64_t kernel_rows, size_t* bytes) {
+    if (n_rows < 0 || kernel_rows <= 0 || kernel_rows > 32 || !bytes)
+        return fail(SC_ERR_INVALID, "invalid tile-source plan size query");
+    *bytes = ts_plan_bytes((n_rows + 127) / 128, (int)kernel_rows);
+    return SC_OK;
+}
+
+int sc_neighbor_tile_sources(const sc_conv_config* cfg, const int32_t* nbr, int64_t n_rows, int64_t n_in,
+                             void* plan, size_t plan_bytes, int32_t* h_max_sources, void* stream) {
+    if (int rc = validate_config(cfg)) return rc;
+    const int64_t K = kernel_rows_of(cfg);
+    if (K > 32) return fail(SC_ERR_UNSUPPORTED, "tile-source plan supports at most 32 kernel offsets");
+    if (n_rows < 0 || n_in < n_rows) return fail(SC_ERR_INVALID, "invalid row counts for the tile-source plan");
+    const int64_t n_tiles = (n_rows + 127) / 128;
+    if (!plan || plan_bytes < ts_plan_bytes(n_tiles, (int)K))
+        return fail(SC_ERR_CAPACITY, "tile-source plan buffer too small: need " +
+                                         std::to_string(ts_plan_bytes(n_tiles, (int)K)) + " bytes");
+    if (!aligned16(plan) || (n_rows && !nbr)) return fail(SC_ERR_INVALID, "null or unaligned pointer");
+    if (n_tiles > 0x7fffffff) return fail(SC_ERR_UNSUPPORTED, "too many row tiles");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    SC_CUDA_TRY(cudaMemsetAsync(plan, 0, 64, st));
+    if (n_tiles > 0) {
+        ts_tile_sources_kernel<<<(unsigned)n_tiles, TSP_THREADS, 0, st>>>(nbr, n_rows, (int)K, n_in, plan, n_tiles);
+        SC_CUDA_TRY(cudaGetLastError());
+    }
+    int32_t h[4] = {0, 0, 0, 0};
+    SC_CUDA_TRY(cudaMemcpyAsync(h, plan, sizeof h, cudaMemcpyDeviceToHost, st));
+    SC_CUDA_TRY(cudaStreamSynchronize(st));
+    if (h_max_sources) *h_max_sources = h[2];
+    if (h[3] > 0)
+        return fail(SC_ERR_CAPACITY, std::to_string(h[3]) + " row tiles read more than " + std::to_string(TS_UMAX) +
+                                         " distinct source rows (largest " + std::to_string(h[2]) + ")");
+    return SC_OK;
+}
+
 static size_t order64_cub_bytes(int64_t n) {
     size_t b = 0;
     cub::DeviceRadixSort::SortPairs(nullptr, b, (const uint64_t*)nullptr, (uint64_t*)nullptr,
@@ -774,6 +892,9 @@ int sc_subm_conv_forward(const sc_conv_config* cfg, sc_dtype dtype, const void* 
     const bool al = aligned16(in) && aligned16(w) && aligned16(out) && aligned16(e.d_out2) &&
                     aligned16(e.d_residual) && aligned16(nbr) && aligned16(e.d_neighbor_rows_ordered) &&
                     aligned16(bias) && aligned16(e.d_ln_gamma) && aligned16(e.d_ln_beta);
+    TsPlan tsp;
+    if (al && aligned16(e.d_tile_sources) && plan_ts(cfg, dtype, e, &tsp))
+        return launch_ts(cfg, in, n_in, n_rows, w, bias, e, out, st, tsp);
     if (al && plan_tc(cfg, dtype, e, &plan))
         return launch_tc(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st, plan);
     if (dtype == SC_DTYPE_F32) return launch_simt<float>(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st);

@@ -209,6 +209,37 @@ def _neighbor_schedule_grouped(config, neighbor_rows, group_mask) -> ConvSchedul
 
 
 @dataclass
+class TileSources:
+    """Tile-source plan of a neighbor map (sc_neighbor_tile_sources): per
+    128-row tile, its distinct source rows and each (row, tap)'s index into
+    them.  Lets 64-channel bf16 convs stage each tile's source rows once."""
+
+    buf: torch.Tensor      # the plan (uint8 device buffer)
+    max_sources: int       # the largest per-tile distinct-row count
+
+
+def neighbor_tile_sources(config: SparseSubmConvConfig, neighbor_rows: torch.Tensor,
+                          n_in: int | None = None) -> "TileSources | None":
+    """The tile-source plan of a map, or None when some tile reads more
+    distinct rows than the kernel stages (the convs then run without it).
+    ``n_in`` is the number of input rows the map addresses (default: its rows)."""
+    _require_cuda("neighbor_rows", neighbor_rows)
+    n = neighbor_rows.shape[0]
+    K = kernel_rows(config)
+    b = ctypes.c_size_t(0)
+    check(lib().sc_neighbor_tile_sources_bytes(n, K, ctypes.byref(b)))
+    buf = torch.empty(max(b.value, 16), dtype=torch.uint8, device=neighbor_rows.device)
+    mx = ctypes.c_int32(0)
+    c = config.c()
+    rc = lib().sc_neighbor_tile_sources(ctypes.byref(c), _ptr(neighbor_rows), n, n if n_in is None else n_in,
+                                        _ptr(buf), b.value, ctypes.byref(mx), _stream(neighbor_rows))
+    if rc == _lib.SC_ERR_CAPACITY:
+        return None
+    check(rc)
+    return TileSources(buf, int(mx.value))
+
+
+@dataclass
 class Epilogue:
     """Fused conv epilogue (see sc_epilogue in include/sparseconv.h).
 
@@ -230,16 +261,19 @@ class Epilogue:
     row_order: torch.Tensor | None = None
     nbr_ordered: torch.Tensor | None = None
     schedule: ConvSchedule | None = None
+    tile_sources: TileSources | None = None
     _keep: list = field(default_factory=list, repr=False)
 
     def c(self) -> ScEpilogue:
         order, ordered = self.row_order, self.nbr_ordered
         if self.schedule is not None:
             order, ordered = self.schedule.order, self.schedule.nbr_ordered
+        ts = self.tile_sources
         return ScEpilogue(_ptr(self.residual), _ptr(self.residual_offset), int(self.residual_repeat),
                           int(self.layer_norm), int(self.ln_width), float(self.ln_eps), _ptr(self.ln_gamma),
                           _ptr(self.ln_beta), int(self.silu), _ptr(self.out2), _ptr(self.out_row_map),
-                          int(self.out_row_map_cols), _ptr(order), _ptr(ordered))
+                          int(self.out_row_map_cols), _ptr(order), _ptr(ordered),
+                          _ptr(ts.buf) if ts is not None else None, int(ts.max_sources) if ts is not None else 0)
 
 
 _DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16}

@@ -234,7 +234,7 @@ class ShardedSubmStack:
     all-to-all) runs on a second stream, then the boundary rows' conv once the
     halo has arrived.  Input and output rows are in Morton-local order."""
 
-    def __init__(self, stack, plan: HaloPlan, schedule: bool = True, _scheds=None):
+    def __init__(self, stack, plan: HaloPlan, schedule: bool = True, _scheds=None, tile_sources: bool = True):
         from . import flex_gmm as F
 
         self.stack = stack      # blocks.SubmStack
@@ -246,11 +246,16 @@ class ShardedSubmStack:
         self.nbr_int = plan.nbr_local[:ni].clone()
         self.nbr_bnd = plan.nbr_local[ni:].clone()
         if _scheds is not None:
-            self.sched_int, self.sched_bnd = _scheds
+            self.sched_int, self.sched_bnd, self.ts_int, self.ts_bnd = _scheds
         else:
-            # conv schedules of the two row sets (tap-mask row order, computed once)
+            # conv schedules of the two row sets (tap-mask row order, computed once), and their
+            # tile-source plans for the 64-input-channel layers
+            n_in = plan.n_local + plan.n_halo
             self.sched_int = F.neighbor_schedule(cfg, self.nbr_int) if ni and schedule else None
             self.sched_bnd = F.neighbor_schedule(cfg, self.nbr_bnd) if plan.n_local > ni and schedule else None
+            want_ts = tile_sources and any(c.in_channels == 64 for c in stack.cfgs)
+            self.ts_int = F.neighbor_tile_sources(cfg, self.nbr_int, n_in) if ni and want_ts else None
+            self.ts_bnd = F.neighbor_tile_sources(cfg, self.nbr_bnd, n_in) if plan.n_local > ni and want_ts else None
         # the last layer writes Morton-local rows directly (epilogue row map: plan row p -> order[p])
         self.order_int = plan.order[:ni].clone()
         self.order_bnd = plan.order[ni:].clone()
@@ -260,7 +265,7 @@ class ShardedSubmStack:
     def twin(self) -> "ShardedSubmStack":
         """A second instance on the same plan and schedules with its own layer
         buffers (e.g. for a second pipelined input slot)."""
-        return ShardedSubmStack(self.stack, self.plan, _scheds=(self.sched_int, self.sched_bnd))
+        return ShardedSubmStack(self.stack, self.plan, _scheds=(self.sched_int, self.sched_bnd, self.ts_int, self.ts_bnd))
 
     def forward(self, x_local: torch.Tensor) -> torch.Tensor:
         """One pass; returns this instance's [n_local, Cout] output buffer (Morton-local rows),
@@ -287,8 +292,9 @@ class ShardedSubmStack:
                 plan.exchange(buf)
                 halo = torch.cuda.Event()
                 halo.record(self.comm)
-            for rows, nbr, sched, order, wait in ((slice(0, ni), self.nbr_int, self.sched_int, self.order_int, False),
-                                                  (slice(ni, n), self.nbr_bnd, self.sched_bnd, self.order_bnd, True)):
+            for rows, nbr, sched, ts, order, wait in (
+                    (slice(0, ni), self.nbr_int, self.sched_int, self.ts_int, self.order_int, False),
+                    (slice(ni, n), self.nbr_bnd, self.sched_bnd, self.ts_bnd, self.order_bnd, True)):
                 if wait:
                     compute.wait_event(halo)
                 if rows.stop <= rows.start:
@@ -298,6 +304,8 @@ class ShardedSubmStack:
                         silu=self.stack.silu, schedule=sched, out_row_map=order, out_row_map_cols=1),
                         out=dst, out_rows=n)
                 else:
-                    F.sparse_subm_conv_forward(cfg, buf, nbr, w, b,
-                                               F.Epilogue(silu=self.stack.silu, schedule=sched), out=dst[rows])
+                    from .blocks import layer_epilogue
+
+                    F.sparse_subm_conv_forward(cfg, buf, nbr, w, b, layer_epilogue(cfg, self.stack.silu, sched, ts),
+                                               out=dst[rows])
         return self.out

@@ -99,7 +99,8 @@ class Cfg5(_Base):
     name = "cfg5_sharded_grid_bf16"
     dtype = "bf16"
 
-    def __init__(self, dev, rank: int = 0, world: int = 1, group=None, seed: int = 0, coords=None, shells: int = 32):
+    def __init__(self, dev, rank: int = 0, world: int = 1, group=None, seed: int = 0, coords=None, shells: int = 32,
+                 tile_sources: bool = True):
         self.dev, self.rank, self.world = dev, rank, world
         self.shells = shells
         coords_np = synth.config5_coords(seed, shells=shells) if coords is None else coords
@@ -119,9 +120,10 @@ class Cfg5(_Base):
             def setup():
                 holder["nbr"] = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct)
                 holder["sched"] = F.neighbor_schedule(cfg, holder["nbr"])
+                holder["ts"] = F.neighbor_tile_sources(cfg, holder["nbr"]) if tile_sources else None
 
             self.setup_ms = _events_ms(setup, dev)
-            self.nbr, self.sched = holder["nbr"], holder["sched"]
+            self.nbr, self.sched, self.tile_sources = holder["nbr"], holder["sched"], holder["ts"]
             self._x = _Slots(lambda k: x_all if k == 0 else x_all.clone())
             self.plan = None
         else:
@@ -129,11 +131,12 @@ class Cfg5(_Base):
 
             def setup():
                 holder["plan"] = sharding.HaloPlan.build_local(ct[self.lo:self.hi].contiguous(), cfg, group)
-                holder["stack"] = sharding.ShardedSubmStack(self.stack, holder["plan"])
+                holder["stack"] = sharding.ShardedSubmStack(self.stack, holder["plan"], tile_sources=tile_sources)
 
             self.setup_ms = _events_ms(setup, dev)
             self.plan = holder["plan"]
             self.nbr = self.plan.nbr_local
+            self.tile_sources = None
             x_mine = x_all[self.lo:self.hi].contiguous()
             del x_all
             self._x = _Slots(lambda k: x_mine if k == 0 else x_mine.clone())
@@ -155,7 +158,7 @@ class Cfg5(_Base):
     def step(self, slot: int = 0) -> torch.Tensor:
         x = self._x[slot]
         if self.world == 1:
-            y = self.stack.forward(x, self.nbr, self.sched)
+            y = self.stack.forward(x, self.nbr, self.sched, self.tile_sources)
         else:
             y = self._sharded[slot].forward(x)
         self._out[slot] = y
@@ -165,7 +168,11 @@ class Cfg5(_Base):
         d = {"workload": self.name, "voxels_total": int(self.n_total), "voxels_this_rank": int(self.n_local),
              "layers": self.launch_labels, "valid_pairs_P_this_rank": int(self.valid_pairs),
              "grid": f"1024^3, union of {self.shells} ellipsoid shells (seed 0)",
-             "step": "4 SubM conv layers (tcgen05, bf16); neighbor map + conv schedule built once per grid",
+             "step": "4 SubM conv layers (tcgen05, bf16); neighbor map, conv schedule and tile-source plan "
+                     "built once per grid",
+             "tile_sources": "64-channel layers stage each tile's distinct source rows once, A built in TMEM"
+             if (self.tile_sources is not None or (self.plan is not None and self._sharded[0].ts_int is not None))
+             else "off",
              "setup_ms": round(self.setup_ms, 3)}
         if self.plan is not None:
             d["halo_rows_this_rank"] = int(self.plan.n_halo)

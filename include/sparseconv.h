@@ -98,6 +98,13 @@ typedef struct sc_epilogue {
                                       tile order (row p = row d_row_order[p]), as written by
                                       sc_neighbor_schedule; lets tiles read their map rows
                                       contiguously */
+    const void* d_tile_sources;    /* nullable: the map's tile-source plan (sc_neighbor_tile_sources);
+                                      with it a bf16 conv of 64 input channels, at most 256
+                                      outputs and a bias/SiLU epilogue gathers each 128-row
+                                      tile's distinct source rows once and builds the taps'
+                                      A operands in tensor memory.  Rows run in map order
+                                      (d_row_order unset).  Changes scheduling only. */
+    int32_t tile_sources_max;      /* the plan's largest per-tile source count (its h_max_sources) */
 } sc_epilogue;
 
 /* ---- library / errors -------------------------------------------------- */
@@ -176,6 +183,20 @@ int sc_neighbor_schedule_grouped_scratch_bytes(int64_t n_rows, size_t* h_bytes);
 int sc_neighbor_schedule_grouped(const sc_conv_config* cfg, const int32_t* d_neighbor_rows, int64_t n_rows,
                                  const uint8_t* d_group_mask8, void* d_scratch, size_t scratch_bytes,
                                  int32_t* d_row_order, int32_t* d_neighbor_rows_ordered, void* stream);
+
+/* Tile-source plan of a neighbor map, computed once and reused by every
+ * conv on the map: for each tile of 128 consecutive map rows, the sorted
+ * distinct valid source rows it reads, a 16-bit index into that list for
+ * every (row, tap), and the tile's tap mask.  On a Morton-ordered surface grid
+ * a tile reads ~8x fewer distinct rows than (row, tap) pairs.  K <= 32.
+ * Synchronises `stream` to read h_max_sources (the largest per-tile count);
+ * returns SC_ERR_CAPACITY if a tile reads more than 576 distinct rows (the
+ * plan is then unusable and convs run without it).  No counterpart in the
+ * reference (a scheduling aid of this library). */
+int sc_neighbor_tile_sources_bytes(int64_t n_rows, int64_t kernel_rows, size_t* h_bytes);
+int sc_neighbor_tile_sources(const sc_conv_config* cfg, const int32_t* d_neighbor_rows, int64_t n_rows,
+                             int64_t n_in, void* d_plan, size_t plan_bytes, int32_t* h_max_sources,
+                             void* stream);
 
 /* ---- convolution ----------------------------------------------------------
  * out[n_rows, Cout] = bias + sum_k sum_c in[nbr[r,k], c] * W[o,k,c]  (+ epilogue)
