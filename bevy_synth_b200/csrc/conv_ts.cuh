@@ -18,19 +18,24 @@
 // of the tile, a 16-bit local index per (row, tap) into that list (0xFFFF =
 // no neighbor), and the tile's tap mask.
 //
-// Warp roles (14 warps, one CTA per SM, persistent, static round-robin over
+// Warp roles (18 warps, one CTA per SM, persistent, static round-robin over
 // (row tile, column tile) pairs -- Morton tiles carry near-uniform work):
 //   0-3   epilogue: TMEM accumulator -> + bias -> [SiLU] -> bf16 rows;
-//   4-7   A builders, one per TMEM sub-partition: thread = tile row; per tap it
-//         reads its row's 128-byte source row from the staging buffer and
-//         stores it as 32 TMEM columns of an A slot;
-//   8-11  staging: cp.async gather of the tile's distinct rows (XOR-swizzled
-//         16-byte chunks) and of its local index block, double-buffered;
-//   12    B loader: one lane issues the weight tile TMA of every tap;
-//   13    MMA: whole warp runs the loop, one elected lane issues
+//   4-11  A builders, two groups of four (one warp per TMEM sub-partition in
+//         each) taking alternate taps: thread = tile row; per tap it reads its
+//         row's 128-byte source row from the staging buffer and stores it as
+//         32 TMEM columns of an A slot (a store and its wait are a latency
+//         chain, so two warps per sub-partition interleave);
+//   12-15 staging: cp.async gather of the tile's distinct rows (XOR-swizzled
+//         16-byte chunks) and of its local index block; double-buffered when
+//         shared memory allows, else single (the A slots give the gather of
+//         the next tile a lead of up to TS_NA taps);
+//   16    B loader: one lane issues the weight tile TMA of every tap;
+//   17    MMA: whole warp runs the loop, one elected lane issues
 //         tcgen05.mma (A from TMEM, M=128, N=tile_n, K=16) and the commits.
-// TMEM: accumulators double-buffered in columns [0, 2*tile_n) (tile_n <= 128),
-// TS_NA A slots of 32 columns in [256, 512).
+// TMEM: accumulators in columns [0, 256) -- double-buffered when tile_n <=
+// 128, one 256-wide accumulator otherwise -- and TS_NA A slots of 32 columns
+// in [256, 512).
 // Every wait is bounded (device wait limit); on expiry the fault word is
 // raised and the roles drain.
 #pragma once
@@ -42,7 +47,8 @@ namespace sc {
 constexpr int TS_UMAX = 576;      // distinct source rows a tile may have (staging capacity bound)
 constexpr int TS_NA = 8;          // A slots in TMEM
 constexpr int TS_A_COL0 = 256;    // first TMEM column of the A slots
-constexpr int TS_THREADS = 14 * 32;
+constexpr int TS_THREADS = 18 * 32;
+constexpr int TS_EPI0 = 0, TS_BLD0 = 4, TS_STG0 = 12, TS_BLOADER = 16, TS_MMA = 17;
 constexpr uint16_t TS_NONE = 0xFFFF;
 
 // ---- prepass: per-tile distinct source rows -----------------------------------
@@ -211,7 +217,9 @@ struct TsParams {
     int silu;
     __nv_bfloat16* out;
     int cout;
-    int tile_n;      // output columns per tile (multiple of 32, <= 128)
+    int tile_n;      // output columns per tile (multiple of 32, <= 256)
+    int n_buf;       // accumulator buffers (2 when tile_n <= 128)
+    int n_stg;       // staging buffers (1 or 2)
     int grid_y;      // column tiles per row tile
     int64_t n_tiles; // row tiles * grid_y
     int u_cap;       // staging rows per buffer (multiple of 8, >= every tile's distinct rows)
@@ -231,13 +239,14 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
                                                ~static_cast<uintptr_t>(1023));
     const int K = p.K;
     const int S = p.b_stages;
+    const int NS = p.n_stg;
     const int B_BYTES = p.tile_n * 128;
     const int stg_units = p.stg_cols / 8;
-    uint8_t* stg = smem;                                                 // [2][u_cap][128]
-    uint8_t* b_smem = stg + 2 * (size_t)p.u_cap * 128;                   // [S][tile_n][128] (1024-aligned)
-    uint8_t* lid_s = b_smem + (size_t)S * B_BYTES;                       // [2][128 * K] uint16
+    uint8_t* stg = smem;                                                 // [NS][u_cap][128]
+    uint8_t* b_smem = stg + NS * (size_t)p.u_cap * 128;                  // [S][tile_n][128] (1024-aligned)
+    uint8_t* lid_s = b_smem + (size_t)S * B_BYTES;                       // [NS][128 * K] uint16
     const int LID_BYTES = 128 * K * 2;
-    uint8_t* epi_s = lid_s + 2 * LID_BYTES;                              // 4 warps of padded staging
+    uint8_t* epi_s = lid_s + NS * LID_BYTES;                             // 4 warps of padded staging
     uint64_t* bars = reinterpret_cast<uint64_t*>(epi_s + 4 * 32 * (stg_units + 1) * 16);
     uint64_t* stg_full = bars;            // [2]
     uint64_t* stg_empty = bars + 2;       // [2]
@@ -260,12 +269,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
     if (tid == 0) {
         for (int b = 0; b < 2; ++b) {
             mbar_init(&stg_full[b], 128);     // every staging thread's cp.async arrive
-            mbar_init(&stg_empty[b], 4);      // the four builder warps
+            mbar_init(&stg_empty[b], 8);      // the eight builder warps
             mbar_init(&tmem_full[b], 1);      // tcgen05.commit after the tile's last MMA
             mbar_init(&tmem_empty[b], 4);     // the four epilogue warps
         }
         for (int s = 0; s < TS_NA; ++s) {
-            mbar_init(&a_full[s], 4);         // the four builder warps
+            mbar_init(&a_full[s], 4);         // the four warps of the slot's builder group
             mbar_init(&a_empty[s], 1);        // tcgen05.commit
         }
         for (int s = 0; s < S; ++s) {
@@ -275,24 +284,24 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         fence_mbar_init();
         fence_proxy_async_smem();
     }
-    if (warp == 13) {
+    if (warp == TS_MMA) {
         tmem_alloc(&misc[0], TC_TMEM_COLS);
         tmem_relinquish();
     }
-    if (warp == 12 && lane == 0) tma_prefetch_desc(&wmap);
+    if (warp == TS_BLOADER && lane == 0) tma_prefetch_desc(&wmap);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = misc[0];
 
-    if (warp >= 8 && warp < 12) {
+    if (warp >= TS_STG0 && warp < TS_STG0 + 4) {
         // ====================================================== staging
-        const int sid = tid - 256;
+        const int sid = tid - TS_STG0 * 32;
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
-            const int sb = (int)(lt & 1);
-            const uint32_t use = (uint32_t)(lt >> 1);
+            const int sb = (int)(lt % NS);
+            const uint32_t use = (uint32_t)(lt / NS);
             if (!mbar_wait(&stg_empty[sb], (use & 1u) ^ 1u)) break;
             const int64_t rt = t / p.grid_y;
             int cnt = __ldg(p.u_count + rt);
@@ -315,23 +324,25 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             cp_async_arrive_noinc(&stg_full[sb]);
         }
         cp_async_wait<0>();
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= TS_BLD0 && warp < TS_BLD0 + 8) {
         // ====================================================== A builders
-        const int q = warp - 4;          // TMEM sub-partition (warp id % 4)
-        const int r = q * 32 + lane;     // tile row == TMEM lane
-        uint32_t a = 0;                  // A slots issued
+        const int q = warp & 3;                 // TMEM sub-partition (warp id % 4)
+        const uint32_t grp = (uint32_t)((warp - TS_BLD0) >> 2);  // taps a with a % 2 == grp
+        const int r = q * 32 + lane;            // tile row == TMEM lane
+        uint32_t a = 0;                         // A slots of the tap sequence (both groups)
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
-            const int sb = (int)(lt & 1);
-            const uint32_t use = (uint32_t)(lt >> 1);
+            const int sb = (int)(lt % NS);
+            const uint32_t use = (uint32_t)(lt / NS);
             if (!__all_sync(0xffffffffu, mbar_wait(&stg_full[sb], use & 1u))) break;
             const int64_t rt = t / p.grid_y;
             const uint32_t mask = ts_mask_of(p, rt);
             const uint16_t* lid = reinterpret_cast<const uint16_t*>(lid_s + sb * LID_BYTES) + r * K;
             const uint8_t* sbase = stg + (size_t)sb * p.u_cap * 128;
             bool ok = true;
-            for (uint32_t m = mask; m; m &= m - 1) {
+            for (uint32_t m = mask; m; m &= m - 1, ++a) {
+                if ((a & 1u) != grp) continue;
                 const int k = __ffs(m) - 1;
                 const int slot = (int)(a % TS_NA);
                 if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[slot], ((a / TS_NA) & 1u) ^ 1u))) {
@@ -359,13 +370,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&a_full[slot]);
-                ++a;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&stg_empty[sb]);  // this warp no longer reads the staged rows
             if (!ok) break;
         }
-    } else if (warp == 12) {
+    } else if (warp == TS_BLOADER) {
         // ====================================================== B loader
         if (lane == 0) {
             int s = 0;
@@ -392,7 +402,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
                 }
             }
         }
-    } else if (warp == 13) {
+    } else if (warp == TS_MMA) {
         // ====================================================== MMA issuer
         const bool issuer = elect_one();
         const uint32_t idesc = umma_idesc_bf16_m128((uint32_t)p.tile_n);
@@ -404,8 +414,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         for (int64_t lt = 0; ok; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
-            const int b = (int)(lt & 1);
-            const uint32_t use = (uint32_t)(lt >> 1);
+            const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
+            const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
             if (!__all_sync(0xffffffffu, mbar_wait(&tmem_empty[b], (use & 1u) ^ 1u))) break;
             tc_fence_after();
             const uint32_t acc = tmem_base + (uint32_t)(b * p.tile_n);
@@ -440,7 +450,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             if (issuer) umma_commit(&tmem_full[b]);
             __syncwarp();
         }
-    } else {
+    } else if (warp < 4) {
         // ====================================================== epilogue
         Staging st;
         st.units = stg_units;
@@ -449,8 +459,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
-            const int b = (int)(lt & 1);
-            const uint32_t use = (uint32_t)(lt >> 1);
+            const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
+            const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
             if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[b], use & 1u))) break;
             tc_fence_after();
             const int64_t rt = t / p.grid_y;
@@ -484,15 +494,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 13) {
+    if (warp == TS_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TC_TMEM_COLS);
     }
 }
 
 // Dynamic shared memory of a launch (1 KB alignment slack included).
-inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int stg_cols) {
-    return 1024 + 2 * (size_t)u_cap * 128 + (size_t)b_stages * tile_n * 128 + 2 * (size_t)128 * K * 2 +
+inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int stg_cols, int n_stg) {
+    return 1024 + (size_t)n_stg * u_cap * 128 + (size_t)b_stages * tile_n * 128 + (size_t)n_stg * 128 * K * 2 +
            4 * 32 * (stg_cols / 8 + 1) * 16 + (size_t)(4 + 2 * TS_NA + 2 * b_stages + 4) * 8 + 16;
 }
 

@@ -407,7 +407,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
 // The tile-source (A-from-TMEM) kernel: bf16, 64 input channels, <= 256 outputs, a plain bias/SiLU
 // epilogue, map rows in order, and a usable tile-source plan.  SC_TS=0 turns it off.
 struct TsPlan {
-    int tile_n, grid_y, u_cap, stages, stg_cols;
+    int tile_n, grid_y, u_cap, stages, stg_cols, n_buf, n_stg;
     size_t smem;
 };
 
@@ -419,21 +419,26 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     if (cin != 64 || K > 32 || cout % 32 != 0 || cout > 256) return false;
     if (e.layer_norm || e.d_residual || e.d_out2 || e.d_out_row_map || e.d_row_order) return false;
     if (e.tile_sources_max < 0 || e.tile_sources_max > TS_UMAX) return false;
-    int tile_n = (int)cout;
-    if (cout > 128) {
-        if (cout % 64 != 0) return false;
-        tile_n = (int)(cout / 2);
-    }
+    // one column tile of all outputs: every tap's A slot is built once; > 128 wide takes the
+    // single 256-column accumulator (its epilogue is not overlapped with the next tile's MMAs)
+    const int tile_n = (int)cout;
     plan->tile_n = tile_n;
-    plan->grid_y = (int)(cout / tile_n);
+    plan->grid_y = 1;
+    plan->n_buf = tile_n <= 128 ? 2 : 1;
     plan->u_cap = std::max(8, (e.tile_sources_max + 7) / 8 * 8);
     plan->stg_cols = tc_stg_cols(tile_n, 64);
-    int S = 8;
-    while (S >= 2 && ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, plan->stg_cols) > kMaxDynSmem) --S;
-    if (S < 2) return false;
-    plan->stages = S;
-    plan->smem = ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, plan->stg_cols);
-    return true;
+    // double-buffered staging with >= 3 weight stages if it fits, else single-buffered staging
+    for (int ns = 2; ns >= 1; --ns) {
+        int S = 8;
+        while (S >= 2 && ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, plan->stg_cols, ns) > kMaxDynSmem) --S;
+        if (S >= 3 || (ns == 1 && S >= 2)) {
+            plan->stages = S;
+            plan->n_stg = ns;
+            plan->smem = ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, plan->stg_cols, ns);
+            return true;
+        }
+    }
+    return false;
 }
 
 static int launch_ts(const sc_conv_config* c, const void* in, int64_t n_in, int64_t n_rows, const void* w,
@@ -469,6 +474,8 @@ static int launch_ts(const sc_conv_config* c, const void* in, int64_t n_in, int6
     p.cout = (int)cout;
     p.tile_n = plan.tile_n;
     p.grid_y = plan.grid_y;
+    p.n_buf = plan.n_buf;
+    p.n_stg = plan.n_stg;
     p.n_tiles = row_tiles * plan.grid_y;
     p.u_cap = plan.u_cap;
     p.b_stages = plan.stages;
