@@ -20,7 +20,8 @@
 //
 // Warp roles (18 warps, one CTA per SM, persistent, static round-robin over
 // (row tile, column tile) pairs -- Morton tiles carry near-uniform work):
-//   0-3   epilogue: TMEM accumulator -> + bias -> [SiLU] -> bf16 rows;
+//   0-3   epilogue: TMEM accumulator -> + bias -> [SiLU] -> bf16 rows (plain
+//         16-byte stores: the TMA unit is left to the weight loads);
 //   4-11  A builders, two groups of four (one warp per TMEM sub-partition in
 //         each) taking alternate taps: thread = tile row; per tap it reads its
 //         row's 128-byte source row from the staging buffer and stores it as
@@ -224,7 +225,6 @@ struct TsParams {
     int64_t n_tiles; // row tiles * grid_y
     int u_cap;       // staging rows per buffer (multiple of 8, >= every tile's distinct rows)
     int b_stages;
-    int stg_cols;    // epilogue staging width
 };
 
 __device__ __forceinline__ uint32_t ts_mask_of(const TsParams& p, int64_t row_tile) {
@@ -241,13 +241,11 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
     const int S = p.b_stages;
     const int NS = p.n_stg;
     const int B_BYTES = p.tile_n * 128;
-    const int stg_units = p.stg_cols / 8;
     uint8_t* stg = smem;                                                 // [NS][u_cap][128]
     uint8_t* b_smem = stg + NS * (size_t)p.u_cap * 128;                  // [S][tile_n][128] (1024-aligned)
     uint8_t* lid_s = b_smem + (size_t)S * B_BYTES;                       // [NS][128 * K] uint16
     const int LID_BYTES = 128 * K * 2;
-    uint8_t* epi_s = lid_s + NS * LID_BYTES;                             // 4 warps of padded staging
-    uint64_t* bars = reinterpret_cast<uint64_t*>(epi_s + 4 * 32 * (stg_units + 1) * 16);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(lid_s + NS * LID_BYTES);
     uint64_t* stg_full = bars;            // [2]
     uint64_t* stg_empty = bars + 2;       // [2]
     uint64_t* a_full = bars + 4;          // [TS_NA]
@@ -452,10 +450,9 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         }
     } else if (warp < 4) {
         // ====================================================== epilogue
-        Staging st;
-        st.units = stg_units;
-        st.swz = 0;
-        st.base = epi_s + warp * 32 * (stg_units + 1) * 16;
+        // Thread = tile row: each 32-column TMEM load becomes four 16-byte global stores of
+        // the row (whole 32-byte sectors).  No bulk/TMA stores: the TMA unit carries the
+        // weight tiles, whose latency the MMA waits on.
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
@@ -466,30 +463,25 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             const int64_t rt = t / p.grid_y;
             const int n0 = (int)(t % p.grid_y) * p.tile_n;
             const int64_t row = rt * 128 + tid;
-            const int64_t orow = row < p.n_rows ? row : -1;
             const uint32_t lane_addr = tmem_base + (uint32_t)(b * p.tile_n) + ((uint32_t)(warp * 32) << 16);
-            for (int g0 = 0; g0 < p.tile_n; g0 += p.stg_cols) {
-                stg_reuse();
-                for (int c = g0; c < g0 + p.stg_cols; c += 32) {
-                    float v[32];
-                    tmem_ld32(lane_addr + c, v);
-                    if (p.bias) add_param32(v, p.bias + n0 + c, false);
-                    if (p.silu) {
+            uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + (row < p.n_rows ? row : 0) * (int64_t)p.cout + n0);
+            for (int c = 0; c < p.tile_n; c += 32) {
+                float v[32];
+                tmem_ld32(lane_addr + c, v);
+                if (p.bias) add_param32(v, p.bias + n0 + c, false);
+                if (p.silu) {
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) v[e] = silu_bf16out(v[e]);
-                    }
-#pragma unroll
-                    for (int qq = 0; qq < 4; ++qq) cvt_store_bf16x8(st.at(lane, (c - g0) / 8 + qq), v + 8 * qq);
+                    for (int e = 0; e < 32; ++e) v[e] = silu_bf16out(v[e]);
                 }
-                __syncwarp();
-                store_staged_rows(st, orow, p.out, p.cout, n0 + g0, lane);
-                __syncwarp();
+                if (row < p.n_rows) {
+#pragma unroll
+                    for (int qq = 0; qq < 4; ++qq) cvt_store_bf16x8(dst + (c + 8 * qq) * 2, v + 8 * qq);
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[b]);
         }
-        bulk_wait_all();
     }
 
     tc_fence_before();
@@ -501,9 +493,9 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 }
 
 // Dynamic shared memory of a launch (1 KB alignment slack included).
-inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int stg_cols, int n_stg) {
+inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int n_stg) {
     return 1024 + (size_t)n_stg * u_cap * 128 + (size_t)b_stages * tile_n * 128 + (size_t)n_stg * 128 * K * 2 +
-           4 * 32 * (stg_cols / 8 + 1) * 16 + (size_t)(4 + 2 * TS_NA + 2 * b_stages + 4) * 8 + 16;
+           (size_t)(4 + 2 * TS_NA + 2 * b_stages + 4) * 8 + 16;
 }
 
 }  // namespace sc
