@@ -294,32 +294,50 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 
     if (warp >= TS_STG0 && warp < TS_STG0 + 4) {
         // ====================================================== staging
+        // 8 lanes per source row (one 16-byte chunk each), 16 rows per pass of the 128 threads.
+        // A thread's row indices are read in batches of 8 independent loads before its copies
+        // (a dependent index load per copy would put one memory latency per row on the path),
+        // and the next tile's row count is read a tile ahead.
         const int sid = tid - TS_STG0 * 32;
-        for (int64_t lt = 0;; ++lt) {
-            const int64_t t = tile_of(lt);
-            if (t < 0) break;
+        const int c = sid & 7;
+        int64_t t = tile_of(0);
+        int cnt_next = t >= 0 ? __ldg(p.u_count + t / p.grid_y) : 0;
+        for (int64_t lt = 0; t >= 0; ++lt) {
             const int sb = (int)(lt % NS);
             const uint32_t use = (uint32_t)(lt / NS);
-            if (!mbar_wait(&stg_empty[sb], (use & 1u) ^ 1u)) break;
             const int64_t rt = t / p.grid_y;
-            int cnt = __ldg(p.u_count + rt);
+            int cnt = cnt_next;
+            const int64_t t_next = tile_of(lt + 1);
+            if (t_next >= 0) cnt_next = __ldg(p.u_count + t_next / p.grid_y);
+            if (!mbar_wait(&stg_empty[sb], (use & 1u) ^ 1u)) break;
             if (cnt > p.u_cap) {  // the host checks the plan's maximum; never taken for a valid plan
                 raise_fault(FAULT_BAD_NEIGHBOR);
                 cnt = p.u_cap;
             }
             const uint32_t base = smem_u32(stg + (size_t)sb * p.u_cap * 128);
-            const int c = sid & 7;
-            for (int u = sid >> 3; u < cnt; u += 16) {
-                int32_t src = __ldg(p.u_rows + rt * TS_UMAX + u);
-                const bool ok = src >= 0 && src < p.n_in;
-                if (!ok) raise_fault(FAULT_BAD_NEIGHBOR);
-                const void* g = ok ? (const void*)(p.in + (int64_t)src * 64 + c * 8) : (const void*)p.in;
-                cp_async_16(base + u * 128 + ((c ^ (u & 7)) << 4), g, ok ? 16u : 0u);
+            const int32_t* urow = p.u_rows + rt * TS_UMAX;
+            for (int u0 = sid >> 3; u0 < cnt; u0 += 16 * 8) {
+                int32_t src[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int u = u0 + 16 * i;
+                    src[i] = u < cnt ? __ldg(urow + u) : -1;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int u = u0 + 16 * i;
+                    if (u >= cnt) break;
+                    const bool ok = src[i] >= 0 && src[i] < p.n_in;
+                    if (!ok) raise_fault(FAULT_BAD_NEIGHBOR);
+                    const void* g = ok ? (const void*)(p.in + (int64_t)src[i] * 64 + c * 8) : (const void*)p.in;
+                    cp_async_16(base + u * 128 + ((c ^ (u & 7)) << 4), g, ok ? 16u : 0u);
+                }
             }
             const uint32_t lbase = smem_u32(lid_s + sb * LID_BYTES);
             const uint8_t* lsrc = reinterpret_cast<const uint8_t*>(p.lidx + rt * 128 * (int64_t)K);
             for (int q = sid; q < LID_BYTES / 16; q += 128) cp_async_16(lbase + q * 16, lsrc + q * 16, 16u);
             cp_async_arrive_noinc(&stg_full[sb]);
+            t = t_next;
         }
         cp_async_wait<0>();
     } else if (warp >= TS_BLD0 && warp < TS_BLD0 + 8) {
@@ -328,14 +346,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         const uint32_t grp = (uint32_t)((warp - TS_BLD0) >> 2);  // taps a with a % 2 == grp
         const int r = q * 32 + lane;            // tile row == TMEM lane
         uint32_t a = 0;                         // A slots of the tap sequence (both groups)
+        uint32_t mask_next = tile_of(0) >= 0 ? ts_mask_of(p, tile_of(0) / p.grid_y) : 0u;
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
             const int sb = (int)(lt % NS);
             const uint32_t use = (uint32_t)(lt / NS);
+            const uint32_t mask = mask_next;   // the tile's tap mask, read a tile ahead
+            if (tile_of(lt + 1) >= 0) mask_next = ts_mask_of(p, tile_of(lt + 1) / p.grid_y);
             if (!__all_sync(0xffffffffu, mbar_wait(&stg_full[sb], use & 1u))) break;
-            const int64_t rt = t / p.grid_y;
-            const uint32_t mask = ts_mask_of(p, rt);
             const uint16_t* lid = reinterpret_cast<const uint16_t*>(lid_s + sb * LID_BYTES) + r * K;
             const uint8_t* sbase = stg + (size_t)sb * p.u_cap * 128;
             bool ok = true;
@@ -379,12 +398,13 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             int s = 0;
             uint32_t ph = 0;
             bool ok = true;
+            uint32_t mask_next = tile_of(0) >= 0 ? ts_mask_of(p, tile_of(0) / p.grid_y) : 0u;
             for (int64_t lt = 0; ok; ++lt) {
                 const int64_t t = tile_of(lt);
                 if (t < 0) break;
-                const int64_t rt = t / p.grid_y;
                 const int n0 = (int)(t % p.grid_y) * p.tile_n;
-                const uint32_t mask = ts_mask_of(p, rt);
+                const uint32_t mask = mask_next;
+                if (tile_of(lt + 1) >= 0) mask_next = ts_mask_of(p, tile_of(lt + 1) / p.grid_y);
                 for (uint32_t m = mask; m; m &= m - 1) {
                     const int k = __ffs(m) - 1;
                     if (!mbar_wait(&b_empty[s], ph ^ 1u)) {
@@ -409,15 +429,17 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         int s = 0;
         uint32_t ph = 0;
         bool ok = true;
+        uint32_t mask_next = tile_of(0) >= 0 ? ts_mask_of(p, tile_of(0) / p.grid_y) : 0u;
         for (int64_t lt = 0; ok; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
             const int b = p.n_buf == 2 ? (int)(lt & 1) : 0;
             const uint32_t use = (uint32_t)(p.n_buf == 2 ? (lt >> 1) : lt);
+            const uint32_t mask = mask_next;
+            if (tile_of(lt + 1) >= 0) mask_next = ts_mask_of(p, tile_of(lt + 1) / p.grid_y);
             if (!__all_sync(0xffffffffu, mbar_wait(&tmem_empty[b], (use & 1u) ^ 1u))) break;
             tc_fence_after();
             const uint32_t acc = tmem_base + (uint32_t)(b * p.tile_n);
-            const uint32_t mask = ts_mask_of(p, t / p.grid_y);
             uint32_t step = 0;
             for (uint32_t m = mask; m; m &= m - 1, ++step) {
                 const int slot = (int)(a % TS_NA);
