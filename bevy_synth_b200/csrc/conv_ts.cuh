@@ -227,6 +227,23 @@ struct TsParams {
     int b_stages;
 };
 
+// Named barrier 1 over the four staging warps (128 threads).
+__device__ __forceinline__ void stg_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The same barrier with an OR reduction: true if `fail` is set in any of the 128 threads,
+// so the staging warps leave their loop together (no thread is left waiting at the barrier).
+__device__ __forceinline__ bool stg_bar_any(bool fail) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)fail)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ uint32_t ts_mask_of(const TsParams& p, int64_t row_tile) {
     const uint32_t m = __ldg(p.tap_mask + row_tile);
     return m ? m : 1u;  // a tile with no valid tap still runs one (all-zero) step
@@ -245,7 +262,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
     uint8_t* b_smem = stg + NS * (size_t)p.u_cap * 128;                  // [S][tile_n][128] (1024-aligned)
     uint8_t* lid_s = b_smem + (size_t)S * B_BYTES;                       // [NS][128 * K] uint16
     const int LID_BYTES = 128 * K * 2;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(lid_s + NS * LID_BYTES);
+    int32_t* ulist = reinterpret_cast<int32_t*>(lid_s + NS * LID_BYTES);   // [2][TS_UMAX] source-row lists
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ulist + 2 * TS_UMAX);
     uint64_t* stg_full = bars;            // [2]
     uint64_t* stg_empty = bars + 2;       // [2]
     uint64_t* a_full = bars + 4;          // [TS_NA]
@@ -295,48 +313,56 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
     if (warp >= TS_STG0 && warp < TS_STG0 + 4) {
         // ====================================================== staging
         // 8 lanes per source row (one 16-byte chunk each), 16 rows per pass of the 128 threads.
-        // A thread's row indices are read in batches of 8 independent loads before its copies
-        // (a dependent index load per copy would put one memory latency per row on the path),
-        // and the next tile's row count is read a tile ahead.
+        // The next tile's source-row list (TS_UMAX int32) is copied into shared memory a tile
+        // ahead (cp.async group + a named barrier of the four staging warps), so the row
+        // copies issue with no dependent global index loads on their path.
         const int sid = tid - TS_STG0 * 32;
         const int c = sid & 7;
+        constexpr int UCHUNKS = TS_UMAX * 4 / 16;
+        auto fetch_list = [&](int64_t tt, int ib) {
+            if (tt < 0) return;
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(p.u_rows + (tt / p.grid_y) * TS_UMAX);
+            const uint32_t dst = smem_u32(ulist + ib * TS_UMAX);
+            for (int q = sid; q < UCHUNKS; q += 128) cp_async_16(dst + q * 16, src + q * 16, 16u);
+        };
         int64_t t = tile_of(0);
+        fetch_list(t, 0);
+        cp_async_commit();
         int cnt_next = t >= 0 ? __ldg(p.u_count + t / p.grid_y) : 0;
+        cp_async_wait<0>();
+        stg_bar_sync();
         for (int64_t lt = 0; t >= 0; ++lt) {
             const int sb = (int)(lt % NS);
             const uint32_t use = (uint32_t)(lt / NS);
+            const int ib = (int)(lt & 1);
             const int64_t rt = t / p.grid_y;
             int cnt = cnt_next;
             const int64_t t_next = tile_of(lt + 1);
+            fetch_list(t_next, ib ^ 1);   // the next tile's list, behind this tile's copies
+            cp_async_commit();
             if (t_next >= 0) cnt_next = __ldg(p.u_count + t_next / p.grid_y);
-            if (!mbar_wait(&stg_empty[sb], (use & 1u) ^ 1u)) break;
-            if (cnt > p.u_cap) {  // the host checks the plan's maximum; never taken for a valid plan
-                raise_fault(FAULT_BAD_NEIGHBOR);
-                cnt = p.u_cap;
-            }
-            const uint32_t base = smem_u32(stg + (size_t)sb * p.u_cap * 128);
-            const int32_t* urow = p.u_rows + rt * TS_UMAX;
-            for (int u0 = sid >> 3; u0 < cnt; u0 += 16 * 8) {
-                int32_t src[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int u = u0 + 16 * i;
-                    src[i] = u < cnt ? __ldg(urow + u) : -1;
+            const bool fail = !mbar_wait(&stg_empty[sb], (use & 1u) ^ 1u);
+            if (!fail) {
+                if (cnt > p.u_cap) {  // the host checks the plan's maximum; never taken for a valid plan
+                    raise_fault(FAULT_BAD_NEIGHBOR);
+                    cnt = p.u_cap;
                 }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int u = u0 + 16 * i;
-                    if (u >= cnt) break;
-                    const bool ok = src[i] >= 0 && src[i] < p.n_in;
+                const uint32_t base = smem_u32(stg + (size_t)sb * p.u_cap * 128);
+                const int32_t* ul = ulist + ib * TS_UMAX;
+                for (int u = sid >> 3; u < cnt; u += 16) {
+                    const int32_t src = ul[u];
+                    const bool ok = src >= 0 && src < p.n_in;
                     if (!ok) raise_fault(FAULT_BAD_NEIGHBOR);
-                    const void* g = ok ? (const void*)(p.in + (int64_t)src[i] * 64 + c * 8) : (const void*)p.in;
+                    const void* g = ok ? (const void*)(p.in + (int64_t)src * 64 + c * 8) : (const void*)p.in;
                     cp_async_16(base + u * 128 + ((c ^ (u & 7)) << 4), g, ok ? 16u : 0u);
                 }
+                const uint32_t lbase = smem_u32(lid_s + sb * LID_BYTES);
+                const uint8_t* lsrc = reinterpret_cast<const uint8_t*>(p.lidx + rt * 128 * (int64_t)K);
+                for (int q = sid; q < LID_BYTES / 16; q += 128) cp_async_16(lbase + q * 16, lsrc + q * 16, 16u);
+                cp_async_arrive_noinc(&stg_full[sb]);
             }
-            const uint32_t lbase = smem_u32(lid_s + sb * LID_BYTES);
-            const uint8_t* lsrc = reinterpret_cast<const uint8_t*>(p.lidx + rt * 128 * (int64_t)K);
-            for (int q = sid; q < LID_BYTES / 16; q += 128) cp_async_16(lbase + q * 16, lsrc + q * 16, 16u);
-            cp_async_arrive_noinc(&stg_full[sb]);
+            cp_async_wait<0>();             // the next tile's list (committed groups; this tile's copies
+            if (stg_bar_any(fail)) break;   // are tracked by the stage barrier), seen by all four warps
             t = t_next;
         }
         cp_async_wait<0>();
@@ -517,7 +543,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 // Dynamic shared memory of a launch (1 KB alignment slack included).
 inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int n_stg) {
     return 1024 + (size_t)n_stg * u_cap * 128 + (size_t)b_stages * tile_n * 128 + (size_t)n_stg * 128 * K * 2 +
-           (size_t)(4 + 2 * TS_NA + 2 * b_stages + 4) * 8 + 16;
+           2 * TS_UMAX * 4 + (size_t)(4 + 2 * TS_NA + 2 * b_stages + 4) * 8 + 16;
 }
 
 }  // namespace sc
