@@ -224,7 +224,8 @@ struct TsParams {
     int grid_y;      // column tiles per row tile
     int64_t n_tiles; // row tiles * grid_y
     int u_cap;       // staging rows per buffer (multiple of 8, >= every tile's distinct rows)
-    int b_stages;
+    int b_stages;    // weight slots (a multiple of grp)
+    int grp;         // taps per pipeline step (G): 4 for tile_n <= 64, else 2
 };
 
 // Named barrier 1 over the four staging warps (128 threads).
@@ -290,7 +291,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             mbar_init(&tmem_empty[b], 4);     // the four epilogue warps
         }
         for (int s = 0; s < TS_NA; ++s) {
-            mbar_init(&a_full[s], 4);         // the four warps of the slot's builder group
+            mbar_init(&a_full[s], 4);         // the four warps of the slot group's builder group
             mbar_init(&a_empty[s], 1);        // tcgen05.commit
         }
         for (int s = 0; s < S; ++s) {
@@ -368,10 +369,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         cp_async_wait<0>();
     } else if (warp >= TS_BLD0 && warp < TS_BLD0 + 8) {
         // ====================================================== A builders
+        // Taps run in steps of G (the tile's taps in mask order, G per step, the last step of a
+        // tile possibly shorter); the two builder groups take alternate steps, each step into
+        // its A slot group (G slots) with one empty wait and one full arrive.
         const int q = warp & 3;                 // TMEM sub-partition (warp id % 4)
-        const uint32_t grp = (uint32_t)((warp - TS_BLD0) >> 2);  // taps a with a % 2 == grp
+        const uint32_t grp = (uint32_t)((warp - TS_BLD0) >> 2);
         const int r = q * 32 + lane;            // tile row == TMEM lane
-        uint32_t a = 0;                         // A slots of the tap sequence (both groups)
+        const int G = p.grp;
+        const uint32_t NAG = (uint32_t)(TS_NA / G);
+        uint32_t stp = 0;                       // steps of the sequence (both groups)
         uint32_t mask_next = tile_of(0) >= 0 ? ts_mask_of(p, tile_of(0) / p.grid_y) : 0u;
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
@@ -384,35 +390,42 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             const uint16_t* lid = reinterpret_cast<const uint16_t*>(lid_s + sb * LID_BYTES) + r * K;
             const uint8_t* sbase = stg + (size_t)sb * p.u_cap * 128;
             bool ok = true;
-            for (uint32_t m = mask; m; m &= m - 1, ++a) {
-                if ((a & 1u) != grp) continue;
-                const int k = __ffs(m) - 1;
-                const int slot = (int)(a % TS_NA);
-                if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[slot], ((a / TS_NA) & 1u) ^ 1u))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();  // the MMAs that read this slot are complete before it is rewritten
-                const uint32_t idx = lid[k];
-                float v[32];
-                if (idx < (uint32_t)p.u_cap) {
-                    const uint8_t* row = sbase + idx * 128;
-#pragma unroll
-                    for (int cc = 0; cc < 8; ++cc) {
-                        const uint4 w4 = *reinterpret_cast<const uint4*>(row + ((cc ^ (idx & 7)) << 4));
-                        v[4 * cc] = __uint_as_float(w4.x);
-                        v[4 * cc + 1] = __uint_as_float(w4.y);
-                        v[4 * cc + 2] = __uint_as_float(w4.z);
-                        v[4 * cc + 3] = __uint_as_float(w4.w);
+            for (uint32_t m = mask; m; ++stp) {
+                const bool mine = (stp & 1u) == grp;
+                const uint32_t ag = stp % NAG;
+                if (mine) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[ag], ((stp / NAG) & 1u) ^ 1u))) {
+                        ok = false;
+                        break;
                     }
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] = 0.f;
+                    tc_fence_after();  // the MMAs that read these slots are complete before they are rewritten
                 }
-                tmem_st32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(TS_A_COL0 + slot * 32), v);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&a_full[slot]);
+                for (int i = 0; i < G && m; ++i, m &= m - 1) {
+                    if (!mine) continue;
+                    const int k = __ffs(m) - 1;
+                    const uint32_t idx = lid[k];
+                    float v[32];
+                    if (idx < (uint32_t)p.u_cap) {
+                        const uint8_t* row = sbase + idx * 128;
+#pragma unroll
+                        for (int cc = 0; cc < 8; ++cc) {
+                            const uint4 w4 = *reinterpret_cast<const uint4*>(row + ((cc ^ (idx & 7)) << 4));
+                            v[4 * cc] = __uint_as_float(w4.x);
+                            v[4 * cc + 1] = __uint_as_float(w4.y);
+                            v[4 * cc + 2] = __uint_as_float(w4.z);
+                            v[4 * cc + 3] = __uint_as_float(w4.w);
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] = 0.f;
+                    }
+                    tmem_st32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(TS_A_COL0 + (ag * G + i) * 32), v);
+                }
+                if (mine) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[ag]);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&stg_empty[sb]);  // this warp no longer reads the staged rows
@@ -420,9 +433,11 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         }
     } else if (warp == TS_BLOADER) {
         // ====================================================== B loader
+        // One weight slot group (G slots, one transaction barrier) per step.
         if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
+            const int G = p.grp;
+            const uint32_t NBG = (uint32_t)(S / G);
+            uint32_t stp = 0;
             bool ok = true;
             uint32_t mask_next = tile_of(0) >= 0 ? ts_mask_of(p, tile_of(0) / p.grid_y) : 0u;
             for (int64_t lt = 0; ok; ++lt) {
@@ -431,18 +446,17 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
                 const int n0 = (int)(t % p.grid_y) * p.tile_n;
                 const uint32_t mask = mask_next;
                 if (tile_of(lt + 1) >= 0) mask_next = ts_mask_of(p, tile_of(lt + 1) / p.grid_y);
-                for (uint32_t m = mask; m; m &= m - 1) {
-                    const int k = __ffs(m) - 1;
-                    if (!mbar_wait(&b_empty[s], ph ^ 1u)) {
+                for (uint32_t m = mask; m; ++stp) {
+                    const uint32_t bg = stp % NBG;
+                    if (!mbar_wait(&b_empty[bg], ((stp / NBG) & 1u) ^ 1u)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&b_full[s], (uint32_t)B_BYTES);
-                    tma_load_3d(smem_u32(b_smem + (size_t)s * B_BYTES), &wmap, &b_full[s], 0, k, n0);
-                    if (++s == S) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
+                    const int g = min(G, __popc(m));
+                    mbar_arrive_expect_tx(&b_full[bg], (uint32_t)(g * B_BYTES));
+                    for (int i = 0; i < g; ++i, m &= m - 1)
+                        tma_load_3d(smem_u32(b_smem + (size_t)(bg * G + i) * B_BYTES), &wmap, &b_full[bg], 0,
+                                    __ffs(m) - 1, n0);
                 }
             }
         }
@@ -451,9 +465,9 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         const bool issuer = elect_one();
         const uint32_t idesc = umma_idesc_bf16_m128((uint32_t)p.tile_n);
         const uint64_t bdesc0 = umma_desc_sw128(smem_u32(b_smem));
-        uint32_t a = 0;
-        int s = 0;
-        uint32_t ph = 0;
+        const int G = p.grp;
+        const uint32_t NAG = (uint32_t)(TS_NA / G), NBG = (uint32_t)(S / G);
+        uint32_t stp = 0;
         bool ok = true;
         uint32_t mask_next = tile_of(0) >= 0 ? ts_mask_of(p, tile_of(0) / p.grid_y) : 0u;
         for (int64_t lt = 0; ok; ++lt) {
@@ -466,31 +480,31 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             if (!__all_sync(0xffffffffu, mbar_wait(&tmem_empty[b], (use & 1u) ^ 1u))) break;
             tc_fence_after();
             const uint32_t acc = tmem_base + (uint32_t)(b * p.tile_n);
-            uint32_t step = 0;
-            for (uint32_t m = mask; m; m &= m - 1, ++step) {
-                const int slot = (int)(a % TS_NA);
-                if (!__all_sync(0xffffffffu, mbar_wait(&a_full[slot], (a / TS_NA) & 1u)) ||
-                    !__all_sync(0xffffffffu, mbar_wait(&b_full[s], ph))) {
+            bool first = true;
+            for (uint32_t m = mask; m; ++stp) {
+                const uint32_t ag = stp % NAG, bg = stp % NBG;
+                if (!__all_sync(0xffffffffu, mbar_wait(&a_full[ag], (stp / NAG) & 1u)) ||
+                    !__all_sync(0xffffffffu, mbar_wait(&b_full[bg], (stp / NBG) & 1u))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t bd = bdesc0 + (uint64_t)((s * B_BYTES) >> 4);
-                const uint32_t at = tmem_base + (uint32_t)(TS_A_COL0 + slot * 32);
+                const int g = min(G, __popc(m));
                 if (issuer) {
+                    for (int i = 0; i < g; ++i) {
+                        const uint64_t bd = bdesc0 + (uint64_t)(((bg * G + i) * B_BYTES) >> 4);
+                        const uint32_t at = tmem_base + (uint32_t)(TS_A_COL0 + (ag * G + i) * 32);
 #pragma unroll
-                    for (int kk = 0; kk < TC_BK / 16; ++kk)
-                        umma_bf16_ts(acc, at + (uint32_t)(kk * 8), bd + (uint64_t)(kk * 2), idesc,
-                                     (step == 0 && kk == 0) ? 0u : 1u);
-                    umma_commit(&a_empty[slot]);
-                    umma_commit(&b_empty[s]);
+                        for (int kk = 0; kk < TC_BK / 16; ++kk)
+                            umma_bf16_ts(acc, at + (uint32_t)(kk * 8), bd + (uint64_t)(kk * 2), idesc,
+                                         (first && i == 0 && kk == 0) ? 0u : 1u);
+                    }
+                    umma_commit(&a_empty[ag]);
+                    umma_commit(&b_empty[bg]);
                 }
                 __syncwarp();
-                ++a;
-                if (++s == S) {
-                    s = 0;
-                    ph ^= 1u;
-                }
+                first = false;
+                for (int i = 0; i < g; ++i) m &= m - 1;
             }
             if (!ok) break;
             if (issuer) umma_commit(&tmem_full[b]);

@@ -407,7 +407,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
 // The tile-source (A-from-TMEM) kernel: bf16, 64 input channels, <= 256 outputs, a plain bias/SiLU
 // epilogue, map rows in order, and a usable tile-source plan.  SC_TS=0 turns it off.
 struct TsPlan {
-    int tile_n, grid_y, u_cap, stages, n_buf, n_stg;
+    int tile_n, grid_y, u_cap, stages, n_buf, n_stg, grp;
     size_t smem;
 };
 
@@ -426,11 +426,15 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     plan->grid_y = 1;
     plan->n_buf = tile_n <= 128 ? 2 : 1;
     plan->u_cap = std::max(8, (e.tile_sources_max + 7) / 8 * 8);
+    // taps per pipeline step: the per-step barrier work is paid once per G taps, which narrow
+    // outputs (little tensor work per tap) need most
+    plan->grp = tile_n <= 64 ? 4 : 2;
     // double-buffered staging with >= 3 weight stages if it fits, else single-buffered staging
     for (int ns = 2; ns >= 1; --ns) {
         int S = 12;
         while (S >= 2 && ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, ns) > kMaxDynSmem) --S;
-        if (S >= 3 || (ns == 1 && S >= 2)) {
+        S = S / plan->grp * plan->grp;  // whole slot groups
+        if (S >= 2 * plan->grp) {
             plan->stages = S;
             plan->n_stg = ns;
             plan->smem = ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, ns);
@@ -478,6 +482,7 @@ static int launch_ts(const sc_conv_config* c, const void* in, int64_t n_in, int6
     p.n_tiles = row_tiles * plan.grid_y;
     p.u_cap = plan.u_cap;
     p.b_stages = plan.stages;
+    p.grp = plan.grp;
     static std::once_flag ts_once;
     static cudaError_t ts_err = cudaSuccess;
     std::call_once(ts_once, [] {
