@@ -419,12 +419,17 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     if (cin != 64 || K > 32 || cout % 32 != 0 || cout > 256) return false;
     if (e.layer_norm || e.d_residual || e.d_out2 || e.d_out_row_map || e.d_row_order) return false;
     if (e.tile_sources_max < 0 || e.tile_sources_max > TS_UMAX) return false;
-    // one column tile of all outputs: every tap's A slot is built once; > 128 wide takes the
-    // single 256-column accumulator (its epilogue is not overlapped with the next tile's MMAs)
-    const int tile_n = (int)cout;
+    // Column tiles of at most 128 outputs with double-buffered accumulators (the epilogue of one
+    // tile overlaps the next tile's MMAs); wider outputs split in two column tiles, each staging
+    // and building its row tile's A operands.
+    int tile_n = (int)cout;
+    if (cout > 128) {
+        if (cout % 64 != 0) return false;
+        tile_n = (int)(cout / 2);
+    }
     plan->tile_n = tile_n;
-    plan->grid_y = 1;
-    plan->n_buf = tile_n <= 128 ? 2 : 1;
+    plan->grid_y = (int)(cout / tile_n);
+    plan->n_buf = 2;
     plan->u_cap = std::max(8, (e.tile_sources_max + 7) / 8 * 8);
     // taps per pipeline step: the per-step barrier work is paid once per G taps, which narrow
     // outputs (little tensor work per tap) need most
