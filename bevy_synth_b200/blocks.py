@@ -200,10 +200,10 @@ class UpsamplePyramid:
 
 
 def layer_epilogue(cfg, silu: bool, schedule=None, tile_sources=None) -> F.Epilogue:
-    """Bias [+ SiLU] epilogue of a plain SubM layer: a 64-input-channel layer runs
-    in map order on the map's tile-source plan when one is given, every other
-    layer on the map's conv schedule."""
-    if tile_sources is not None and cfg.in_channels == 64:
+    """Bias [+ SiLU] epilogue of a plain SubM layer: a layer of 64 input and at
+    most 128 output channels runs in map order on the map's tile-source plan
+    when one is given, every other layer on the map's conv schedule."""
+    if tile_sources is not None and cfg.in_channels == 64 and cfg.out_channels <= 128:
         return F.Epilogue(silu=silu, tile_sources=tile_sources)
     return F.Epilogue(silu=silu, schedule=schedule)
 

@@ -404,7 +404,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
     return SC_OK;
 }
 
-// The tile-source (A-from-TMEM) kernel: bf16, 64 input channels, <= 256 outputs, a plain bias/SiLU
+// The tile-source (A-from-TMEM) kernel: bf16, 64 input channels, <= 128 outputs, a plain bias/SiLU
 // epilogue, map rows in order, and a usable tile-source plan.  SC_TS=0 turns it off.
 struct TsPlan {
     int tile_n, grid_y, u_cap, stages, n_buf, n_stg, grp;
@@ -416,19 +416,17 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     if (const char* env = std::getenv("SC_TS"))
         if (env[0] == '0') return false;
     const int64_t K = kernel_rows_of(c), cin = c->in_channels, cout = c->out_channels;
-    if (cin != 64 || K > 32 || cout % 32 != 0 || cout > 256) return false;
+    if (cin != 64 || K > 32 || cout % 32 != 0) return false;
     if (e.layer_norm || e.d_residual || e.d_out2 || e.d_out_row_map || e.d_row_order) return false;
     if (e.tile_sources_max < 0 || e.tile_sources_max > TS_UMAX) return false;
-    // Column tiles of at most 128 outputs with double-buffered accumulators (the epilogue of one
-    // tile overlaps the next tile's MMAs); wider outputs split in two column tiles, each staging
-    // and building its row tile's A operands.
-    int tile_n = (int)cout;
-    if (cout > 128) {
-        if (cout % 64 != 0) return false;
-        tile_n = (int)(cout / 2);
-    }
+    // One column tile of at most 128 outputs, accumulators double-buffered (the epilogue of one
+    // tile overlaps the next tile's MMAs).  Wider outputs stay on the generic kernel: measured on
+    // config 5's 64->256 layer, one 256-wide single-buffered accumulator (6.3 ms) and two 128-wide
+    // column tiles that stage and build A twice (7.8 ms) both lost to it (5.8 ms).
+    if (cout > 128) return false;
+    const int tile_n = (int)cout;
     plan->tile_n = tile_n;
-    plan->grid_y = (int)(cout / tile_n);
+    plan->grid_y = 1;
     plan->n_buf = 2;
     plan->u_cap = std::max(8, (e.tile_sources_max + 7) / 8 * 8);
     // taps per pipeline step: the per-step barrier work is paid once per G taps, which narrow

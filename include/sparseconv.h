@@ -99,7 +99,7 @@ typedef struct sc_epilogue {
                                       sc_neighbor_schedule; lets tiles read their map rows
                                       contiguously */
     const void* d_tile_sources;    /* nullable: the map's tile-source plan (sc_neighbor_tile_sources);
-                                      with it a bf16 conv of 64 input channels, at most 256
+                                      with it a bf16 conv of 64 input channels, at most 128
                                       outputs and a bias/SiLU epilogue gathers each 128-row
                                       tile's distinct source rows once and builds the taps'
                                       A operands in tensor memory.  Rows run in map order

@@ -60,7 +60,7 @@ def test_plan_describes_the_map(cuda_device):
     assert_no_fault()
 
 
-@pytest.mark.parametrize("cout,silu", [(64, False), (96, True), (128, False), (192, True), (256, False)])
+@pytest.mark.parametrize("cout,silu", [(64, False), (96, True), (128, False), (32, True)])
 def test_tile_source_conv_equals_generic_kernel(cuda_device, monkeypatch, cout, silu):
     coords = shell()
     n = coords.shape[0]
@@ -71,6 +71,7 @@ def test_tile_source_conv_equals_generic_kernel(cuda_device, monkeypatch, cout, 
     cfg = F.SparseSubmConvConfig.subm3(64, cout)
     nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords))
     ts = F.neighbor_tile_sources(cfg, nbr)
+    assert ts is not None
     xd, wd, bd = to_dev(x, torch.bfloat16), to_dev(w, torch.bfloat16), to_dev(b)
     got = F.sparse_subm_conv_forward(cfg, xd, nbr, wd, bd, F.Epilogue(silu=silu, tile_sources=ts))
     monkeypatch.setenv("SC_TC_PAIR", "0")   # the single-CTA generic kernel, same tile rows
@@ -98,7 +99,8 @@ def test_plan_over_capacity_falls_back(cuda_device):
 
 def test_config5_grid_layers_on_tile_sources(cuda_device):
     """Config 5's 64-channel layers (7.07M rows) through the tile-source plan agree with the
-    generic kernel's results to rounding."""
+    generic kernel's results to rounding (64->64 takes the tile-source kernel; 64->256, wider
+    than it takes, runs on the generic kernel with the plan ignored)."""
     from bevy_synth_b200.workloads import Cfg5
     wl = Cfg5(torch.device("cuda:0"))
     assert wl.tile_sources is not None and wl.tile_sources.max_sources <= UMAX
