@@ -1,4 +1,4 @@
-"""Multi-GPU paths on 2 GPUs (skipped with fewer): Morton-range sharding with
+"""Multi-GPU paths on 2 and 4 GPUs (each skipped with fewer): Morton-range sharding with
 the NCCL halo exchange and asset sharding, each against the whole input on
 one GPU (tests/multi_gpu_check.py under torchrun)."""
 import json
@@ -22,14 +22,15 @@ def _port():
     return p
 
 
-def test_two_gpu_sharding_matches_single_gpu():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharding_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(_port()),
            os.path.join(HERE, "multi_gpu_check.py")]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     lines = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
-    assert len(lines) == 2 and all(l["ok"] for l in lines), lines
+    assert len(lines) == world and all(l["ok"] for l in lines), lines
