@@ -30,13 +30,12 @@
 //   12-15 staging: cp.async gather of the tile's distinct rows (XOR-swizzled
 //         16-byte chunks) and of its local index block; double-buffered when
 //         shared memory allows, else single (the A slots give the gather of
-//         the next tile a lead of up to TS_NA taps);
+//         the next tile a lead of up to the A slots' taps);
 //   16    B loader: one lane issues the weight tile TMA of every tap;
 //   17    MMA: whole warp runs the loop, one elected lane issues
 //         tcgen05.mma (A from TMEM, M=128, N=tile_n, K=16) and the commits.
-// TMEM: accumulators in columns [0, 256) -- double-buffered when tile_n <=
-// 128, one 256-wide accumulator otherwise -- and TS_NA A slots of 32 columns
-// in [256, 512).
+// TMEM: double-buffered accumulators in columns [0, 2 tile_n) and the A slots
+// (32 columns each) in the rest: 12 for 64 outputs, 8 for 128.
 // Every wait is bounded (device wait limit); on expiry the fault word is
 // raised and the roles drain.
 #pragma once
@@ -46,8 +45,7 @@
 namespace sc {
 
 constexpr int TS_UMAX = 576;      // distinct source rows a tile may have (staging capacity bound)
-constexpr int TS_NA = 8;          // A slots in TMEM
-constexpr int TS_A_COL0 = 256;    // first TMEM column of the A slots
+constexpr int TS_NA_MAX = 12;     // A slots in TMEM (32 columns each) at most
 constexpr int TS_THREADS = 18 * 32;
 constexpr int TS_EPI0 = 0, TS_BLD0 = 4, TS_STG0 = 12, TS_BLOADER = 16, TS_MMA = 17;
 constexpr uint16_t TS_NONE = 0xFFFF;
@@ -226,6 +224,8 @@ struct TsParams {
     int u_cap;       // staging rows per buffer (multiple of 8, >= every tile's distinct rows)
     int b_stages;    // weight slots (a multiple of grp)
     int grp;         // taps per pipeline step (G): 4 for tile_n <= 64, else 2
+    int n_a;         // A slots (a multiple of grp, <= TS_NA_MAX)
+    int a_col0;      // first TMEM column of the A slots (n_buf * tile_n)
 };
 
 // Named barrier 1 over the four staging warps (128 threads).
@@ -267,9 +267,9 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
     uint64_t* bars = reinterpret_cast<uint64_t*>(ulist + 2 * TS_UMAX);
     uint64_t* stg_full = bars;            // [2]
     uint64_t* stg_empty = bars + 2;       // [2]
-    uint64_t* a_full = bars + 4;          // [TS_NA]
-    uint64_t* a_empty = a_full + TS_NA;   // [TS_NA]
-    uint64_t* b_full = a_empty + TS_NA;   // [S]
+    uint64_t* a_full = bars + 4;              // [TS_NA_MAX]
+    uint64_t* a_empty = a_full + TS_NA_MAX;   // [TS_NA_MAX]
+    uint64_t* b_full = a_empty + TS_NA_MAX;   // [S]
     uint64_t* b_empty = b_full + S;       // [S]
     uint64_t* tmem_full = b_empty + S;    // [2]
     uint64_t* tmem_empty = tmem_full + 2; // [2]
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             mbar_init(&tmem_full[b], 1);      // tcgen05.commit after the tile's last MMA
             mbar_init(&tmem_empty[b], 4);     // the four epilogue warps
         }
-        for (int s = 0; s < TS_NA; ++s) {
+        for (int s = 0; s < TS_NA_MAX; ++s) {
             mbar_init(&a_full[s], 4);         // the four warps of the slot group's builder group
             mbar_init(&a_empty[s], 1);        // tcgen05.commit
         }
@@ -371,12 +371,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         // ====================================================== A builders
         // Taps run in steps of G (the tile's taps in mask order, G per step, the last step of a
         // tile possibly shorter); the two builder groups take alternate steps, each step into
-        // its A slot group (G slots) with one empty wait and one full arrive.
+        // the next of the n_a / G slot groups, with one empty wait and one full arrive.  A step's
+        // TMEM stores are issued back to back and completed by one wait before the arrive, so
+        // the shared-memory reads of a tap overlap the previous tap's store.
         const int q = warp & 3;                 // TMEM sub-partition (warp id % 4)
         const uint32_t grp = (uint32_t)((warp - TS_BLD0) >> 2);
         const int r = q * 32 + lane;            // tile row == TMEM lane
         const int G = p.grp;
-        const uint32_t NAG = (uint32_t)(TS_NA / G);
+        const uint32_t NAG = (uint32_t)(p.n_a / G);
+        const uint32_t lane_cols = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)p.a_col0;
         uint32_t stp = 0;                       // steps of the sequence (both groups)
         uint32_t mask_next = tile_of(0) >= 0 ? ts_mask_of(p, tile_of(0) / p.grid_y) : 0u;
         for (int64_t lt = 0;; ++lt) {
@@ -391,17 +394,18 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             const uint8_t* sbase = stg + (size_t)sb * p.u_cap * 128;
             bool ok = true;
             for (uint32_t m = mask; m; ++stp) {
-                const bool mine = (stp & 1u) == grp;
-                const uint32_t ag = stp % NAG;
-                if (mine) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[ag], ((stp / NAG) & 1u) ^ 1u))) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();  // the MMAs that read these slots are complete before they are rewritten
+                if ((stp & 1u) != grp) {        // the other group's step: skip its taps
+                    for (int i = 0; i < G && m; ++i) m &= m - 1;
+                    continue;
                 }
+                const uint32_t ag = stp % NAG;
+                if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[ag], ((stp / NAG) & 1u) ^ 1u))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();  // the MMAs that read these slots are complete before they are rewritten
+#pragma unroll 1
                 for (int i = 0; i < G && m; ++i, m &= m - 1) {
-                    if (!mine) continue;
                     const int k = __ffs(m) - 1;
                     const uint32_t idx = lid[k];
                     float v[32];
@@ -419,13 +423,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 #pragma unroll
                         for (int e = 0; e < 32; ++e) v[e] = 0.f;
                     }
-                    tmem_st32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(TS_A_COL0 + (ag * G + i) * 32), v);
+                    tmem_st32_async(lane_cols + (uint32_t)((ag * G + i) * 32), v);
                 }
-                if (mine) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[ag]);
-                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[ag]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&stg_empty[sb]);  // this warp no longer reads the staged rows
@@ -466,7 +469,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         const uint32_t idesc = umma_idesc_bf16_m128((uint32_t)p.tile_n);
         const uint64_t bdesc0 = umma_desc_sw128(smem_u32(b_smem));
         const int G = p.grp;
-        const uint32_t NAG = (uint32_t)(TS_NA / G), NBG = (uint32_t)(S / G);
+        const uint32_t NAG = (uint32_t)(p.n_a / G), NBG = (uint32_t)(S / G);
         uint32_t stp = 0;
         bool ok = true;
         uint32_t mask_next = tile_of(0) >= 0 ? ts_mask_of(p, tile_of(0) / p.grid_y) : 0u;
@@ -493,7 +496,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
                 if (issuer) {
                     for (int i = 0; i < g; ++i) {
                         const uint64_t bd = bdesc0 + (uint64_t)(((bg * G + i) * B_BYTES) >> 4);
-                        const uint32_t at = tmem_base + (uint32_t)(TS_A_COL0 + (ag * G + i) * 32);
+                        const uint32_t at = tmem_base + (uint32_t)(p.a_col0 + (ag * G + i) * 32);
 #pragma unroll
                         for (int kk = 0; kk < TC_BK / 16; ++kk)
                             umma_bf16_ts(acc, at + (uint32_t)(kk * 8), bd + (uint64_t)(kk * 2), idesc,
@@ -557,7 +560,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 // Dynamic shared memory of a launch (1 KB alignment slack included).
 inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int n_stg) {
     return 1024 + (size_t)n_stg * u_cap * 128 + (size_t)b_stages * tile_n * 128 + (size_t)n_stg * 128 * K * 2 +
-           2 * TS_UMAX * 4 + (size_t)(4 + 2 * TS_NA + 2 * b_stages + 4) * 8 + 16;
+           2 * TS_UMAX * 4 + (size_t)(4 + 2 * TS_NA_MAX + 2 * b_stages + 4) * 8 + 16;
 }
 
 }  // namespace sc

@@ -158,7 +158,8 @@ static int sm_count() {
 }
 
 // Decides whether the tensor-core kernel takes this conv and with which tiling.
-static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, TcPlan* plan) {
+// n_rows < 0: row count unknown (no column split for small grids).
+static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, TcPlan* plan, int64_t n_rows) {
     if (dt != SC_DTYPE_BF16 || c->groups != 1 || force_simt()) return false;
     const int64_t K = kernel_rows_of(c), cin = c->in_channels, cout = c->out_channels;
     if (K > TC_MAX_K || cin % 8 != 0 || cin < 64 || cout % 32 != 0) return false;
@@ -184,6 +185,16 @@ static bool plan_tc(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
         int64_t n_tiles = (cout + cap - 1) / cap;
         while (cout % n_tiles != 0 || (cout / n_tiles) % 32 != 0) ++n_tiles;
         tile_n = (int)(cout / n_tiles);
+        // A grid with fewer (row, column) tiles than SMs leaves SMs idle: halve the column tile
+        // while it stays a multiple of 32 (a launch of one tile per SM is as long as its slowest
+        // tile, so narrower tiles on more SMs finish sooner).  SC_TC_SPLIT=0 turns it off.
+        const char* split_env = std::getenv("SC_TC_SPLIT");
+        if (n_rows > 0 && !(split_env && split_env[0] == '0')) {
+            const int64_t row_tiles = (n_rows + 127) / 128;
+            while (row_tiles * (cout / tile_n) < sm_count() && tile_n >= 128 && (tile_n / 2) % 32 == 0 &&
+                   cout % (tile_n / 2) == 0)
+                tile_n /= 2;
+        }
     }
     if (tile_n > 512 || tile_n % 32 != 0) return false;
     const int64_t W = (e.layer_norm && e.ln_width) ? e.ln_width : tile_n;
@@ -407,7 +418,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
 // The tile-source (A-from-TMEM) kernel: bf16, 64 input channels, <= 128 outputs, a plain bias/SiLU
 // epilogue, map rows in order, and a usable tile-source plan.  SC_TS=0 turns it off.
 struct TsPlan {
-    int tile_n, grid_y, u_cap, stages, n_buf, n_stg, grp;
+    int tile_n, grid_y, u_cap, stages, n_buf, n_stg, grp, n_a, a_col0;
     size_t smem;
 };
 
@@ -423,15 +434,27 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     // tile overlaps the next tile's MMAs).  Wider outputs stay on the generic kernel: measured on
     // config 5's 64->256 layer, one 256-wide single-buffered accumulator (6.3 ms) and two 128-wide
     // column tiles that stage and build A twice (7.8 ms) both lost to it (5.8 ms).
-    if (cout > 128) return false;
-    const int tile_n = (int)cout;
+    // SC_TS_WIDE=1 (one single-buffered accumulator up to 256 wide) and SC_TS_WIDE=2 (128-wide
+    // column tiles, each staging and building A again) opt wider outputs in.
+    const char* wide_env = std::getenv("SC_TS_WIDE");
+    const int wide = wide_env ? wide_env[0] - '0' : 0;
+    int tile_n = (int)cout;
+    if (cout > 128) {
+        if (wide == 1 && cout <= 256) tile_n = (int)cout;
+        else if (wide == 2 && cout % 128 == 0) tile_n = 128;
+        else return false;
+    }
     plan->tile_n = tile_n;
-    plan->grid_y = 1;
-    plan->n_buf = 2;
+    plan->grid_y = (int)(cout / tile_n);
+    plan->n_buf = tile_n <= 128 ? 2 : 1;
     plan->u_cap = std::max(8, (e.tile_sources_max + 7) / 8 * 8);
     // taps per pipeline step: the per-step barrier work is paid once per G taps, which narrow
     // outputs (little tensor work per tap) need most
     plan->grp = tile_n <= 64 ? 4 : 2;
+    // A slots: the TMEM columns the two accumulators leave, whole slot groups of G
+    plan->a_col0 = plan->n_buf * tile_n;
+    plan->n_a = std::min(TS_NA_MAX, ((int)TC_TMEM_COLS - plan->a_col0) / 32) / plan->grp * plan->grp;
+    if (plan->n_a < 2 * plan->grp) return false;
     // double-buffered staging with >= 3 weight stages if it fits, else single-buffered staging
     for (int ns = 2; ns >= 1; --ns) {
         int S = 12;
@@ -486,6 +509,8 @@ static int launch_ts(const sc_conv_config* c, const void* in, int64_t n_in, int6
     p.u_cap = plan.u_cap;
     p.b_stages = plan.stages;
     p.grp = plan.grp;
+    p.n_a = plan.n_a;
+    p.a_col0 = plan.a_col0;
     static std::once_flag ts_once;
     static cudaError_t ts_err = cudaSuccess;
     std::call_once(ts_once, [] {
@@ -868,7 +893,7 @@ int sc_conv_uses_tensor_cores(const sc_conv_config* cfg, sc_dtype dtype, int32_t
     sc_epilogue e;
     memset(&e, 0, sizeof e);
     TcPlan plan;
-    *flag = plan_tc(cfg, dtype, e, &plan) ? 1 : 0;
+    *flag = plan_tc(cfg, dtype, e, &plan, -1) ? 1 : 0;
     return SC_OK;
 }
 
@@ -908,7 +933,7 @@ int sc_subm_conv_forward(const sc_conv_config* cfg, sc_dtype dtype, const void* 
     TsPlan tsp;
     if (al && aligned16(e.d_tile_sources) && plan_ts(cfg, dtype, e, &tsp))
         return launch_ts(cfg, in, n_in, n_rows, w, bias, e, out, st, tsp);
-    if (al && plan_tc(cfg, dtype, e, &plan))
+    if (al && plan_tc(cfg, dtype, e, &plan, n_rows))
         return launch_tc(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st, plan);
     if (dtype == SC_DTYPE_F32) return launch_simt<float>(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st);
     return launch_simt<__nv_bfloat16>(cfg, in, n_in, nbr, n_rows, w, bias, e, out, st);

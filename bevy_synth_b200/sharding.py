@@ -212,12 +212,20 @@ class HaloPlan:
         """A [n_local + n_halo, C] layer buffer in plan order: the convs write rows [0, n_local)."""
         return torch.empty((self.n_local + self.n_halo, channels), dtype=dtype, device=device)
 
-    def exchange(self, buf: torch.Tensor, gather_fn: GatherFn = _default_gather) -> torch.Tensor:
-        """Fills buf[n_local:] with the halo rows, packing buf[:n_local] rows for the peers."""
+    def pack(self, buf: torch.Tensor, gather_fn: GatherFn = _default_gather) -> torch.Tensor:
+        """The rows of buf[:n_local] the peers read, grouped by destination rank.  They are
+        all boundary rows (plan rows >= n_interior)."""
         n = self.n_local
-        send = gather_fn(buf[:n], self.send_idx) if self.send_idx.numel() else buf.new_empty((0,) + buf.shape[1:])
-        recv = buf[n:]
-        dist.all_to_all_single(recv, send.contiguous(), output_split_sizes=self.recv_counts,
+        if not self.send_idx.numel():
+            return buf.new_empty((0,) + buf.shape[1:])
+        return gather_fn(buf[:n], self.send_idx).contiguous()
+
+    def exchange(self, buf: torch.Tensor, gather_fn: GatherFn = _default_gather, send=None) -> torch.Tensor:
+        """Fills buf[n_local:] with the halo rows, packing buf[:n_local] rows for the peers
+        (or sending ``send``, an earlier ``pack`` of buf)."""
+        if send is None:
+            send = self.pack(buf, gather_fn)
+        dist.all_to_all_single(buf[self.n_local:], send, output_split_sizes=self.recv_counts,
                                input_split_sizes=self.send_counts, group=self.group)
         return buf
 
@@ -229,10 +237,14 @@ class HaloPlan:
 
 
 class ShardedSubmStack:
-    """SubM layer stack on a Morton-range-sharded grid.  Per layer: the
-    interior rows' conv on the compute stream while the halo exchange (pack +
-    all-to-all) runs on a second stream, then the boundary rows' conv once the
-    halo has arrived.  Input and output rows are in Morton-local order."""
+    """SubM layer stack on a Morton-range-sharded grid.  Every row a peer reads
+    is a boundary row, so a layer runs its boundary rows' conv first; the next
+    layer's halo exchange (pack + all-to-all, second stream) then overlaps this
+    layer's interior rows' conv, and the next layer's boundary conv starts as
+    soon as both are done.  Only the first layer's exchange (the input rows)
+    is exposed.  The interior conv is released once the pack has run, so the
+    all-to-all is already in flight when the conv's CTAs occupy the SMs.
+    Input and output rows are in Morton-local order."""
 
     def __init__(self, stack, plan: HaloPlan, schedule: bool = True, _scheds=None, tile_sources: bool = True):
         from . import flex_gmm as F
@@ -280,23 +292,38 @@ class ShardedSubmStack:
             self.comm = torch.cuda.Stream(dev)
         compute = torch.cuda.current_stream(dev)
         F.gather_rows(x_local, plan.order, out=self.bufs[0][:n])
-        layers = list(zip(self.stack.cfgs, self.stack.w, self.stack.b))
-        for i, (cfg, w, b) in enumerate(layers):
-            buf = self.bufs[i]
-            last = i + 1 == len(layers)
-            dst = self.out if last else self.bufs[i + 1][:n]
+
+        def exchange(buf):
+            """Pack + all-to-all of ``buf``'s boundary rows on the comm stream, after the
+            compute stream's work so far; returns the (packed, halo arrived) events."""
             ready = torch.cuda.Event()
             ready.record(compute)
             with torch.cuda.stream(self.comm):
                 self.comm.wait_event(ready)
-                plan.exchange(buf)
-                halo = torch.cuda.Event()
-                halo.record(self.comm)
-            for rows, nbr, sched, ts, order, wait in (
-                    (slice(0, ni), self.nbr_int, self.sched_int, self.ts_int, self.order_int, False),
-                    (slice(ni, n), self.nbr_bnd, self.sched_bnd, self.ts_bnd, self.order_bnd, True)):
-                if wait:
+                send = plan.pack(buf)
+                packed = torch.cuda.Event()
+                packed.record(self.comm)
+                plan.exchange(buf, send=send)
+                arrived = torch.cuda.Event()
+                arrived.record(self.comm)
+            return packed, arrived
+
+        layers = list(zip(self.stack.cfgs, self.stack.w, self.stack.b))
+        _, halo = exchange(self.bufs[0])
+        for i, (cfg, w, b) in enumerate(layers):
+            buf = self.bufs[i]
+            last = i + 1 == len(layers)
+            dst = self.out if last else self.bufs[i + 1][:n]
+            packed = None
+            for rows, nbr, sched, ts, order, boundary in (
+                    (slice(ni, n), self.nbr_bnd, self.sched_bnd, self.ts_bnd, self.order_bnd, True),
+                    (slice(0, ni), self.nbr_int, self.sched_int, self.ts_int, self.order_int, False)):
+                if boundary:
                     compute.wait_event(halo)
+                elif not last:
+                    # the next layer's halo: its rows are this layer's boundary outputs
+                    packed, halo = exchange(self.bufs[i + 1])
+                    compute.wait_event(packed)
                 if rows.stop <= rows.start:
                     continue
                 if last:  # rows go straight to their Morton-local place
