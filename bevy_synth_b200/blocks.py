@@ -134,6 +134,7 @@ class C2SUpsampleBlock:
         self.cfg1 = F.SparseSubmConvConfig.subm3(self.cin, 8 * self.cout)
         self.cfg2 = F.SparseSubmConvConfig.subm3(self.cout, self.cout)
         self.group_children = True
+        self.schedule_children = True
 
     def forward(self, coords: torch.Tensor, x: torch.Tensor, mask: torch.Tensor | None = None, nbr_parent=None,
                 threshold: float = 0.0, keep: dict | None = None):
@@ -141,7 +142,9 @@ class C2SUpsampleBlock:
         children come from the to_subdiv head on x (logits > threshold).  With
         ``keep`` (a dict) the intermediates are left in it: ``h`` (parents after
         LN + SiLU), ``h_up`` (children after conv1's LN + SiLU epilogue),
-        ``child_row`` ([Np, 8] child of each parent block), ``nbr_parent``."""
+        ``child_row`` ([Np, 8] child of each parent block), ``nbr_parent``,
+        ``sched_child`` (the child map's conv schedule, for the convs that
+        follow on the children; None when ``schedule_children`` is off)."""
         p = self.p
         if mask is None:
             if p.w_sub is None:
@@ -162,12 +165,15 @@ class C2SUpsampleBlock:
                        out_row_map=child_row, out_row_map_cols=8, schedule=sched1),
             out_rows=n_child)
         nbr_child = F.neighbor_rows_tensor_from_coords_tensor(self.cfg2, child_coords)
+        # the child grid is sparse (config 3: ~7 of 27 taps per row): grouping rows by tap mask
+        # halves the executed MMA work of conv2 and of the ResBlock convs that follow
+        sched2 = F.neighbor_schedule(self.cfg2, nbr_child) if self.schedule_children and n_child else None
         rep = self.cout // (self.cin // 8)
         y = F.sparse_subm_conv_forward(
             self.cfg2, h_up, nbr_child, p.w2, p.b2,
-            F.Epilogue(residual=x, residual_offset=skip_off, residual_repeat=rep))
+            F.Epilogue(residual=x, residual_offset=skip_off, residual_repeat=rep, schedule=sched2))
         if keep is not None:
-            keep.update(h=h, h_up=h_up, child_row=child_row, nbr_parent=nbr_parent)
+            keep.update(h=h, h_up=h_up, child_row=child_row, nbr_parent=nbr_parent, sched_child=sched2)
         return child_coords, y, nbr_child
 
     def flops(self, nbr_parent: torch.Tensor, nbr_child: torch.Tensor, mask: torch.Tensor) -> float:
@@ -193,8 +199,9 @@ class UpsamplePyramid:
     def forward(self, coords: torch.Tensor, x: torch.Tensor, masks: list[torch.Tensor]):
         stats = []
         for (c2s, res, _), mask in zip(self.levels, masks):
-            coords, x, nbr = c2s.forward(coords, x, mask)
-            x = res.forward(x, nbr)
+            keep: dict = {}
+            coords, x, nbr = c2s.forward(coords, x, mask, keep=keep)
+            x = res.forward(x, nbr, schedule=keep["sched_child"])
             stats.append((coords.shape[0], nbr))
         return coords, x, stats
 

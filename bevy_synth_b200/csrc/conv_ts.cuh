@@ -20,9 +20,8 @@
 //
 // Warp roles (18 warps, one CTA per SM, persistent, static round-robin over
 // (row tile, column tile) pairs -- Morton tiles carry near-uniform work):
-//   0-3   epilogue: TMEM accumulator -> + bias -> [SiLU] -> bf16 rows, through a
-//         per-warp transpose buffer so that stores write whole sectors (the TMA
-//         unit is left to the weight loads);
+//   0-3   epilogue: TMEM accumulator -> + bias -> [SiLU] -> bf16 rows (plain
+//         16-byte stores: the TMA unit is left to the weight loads);
 //   4-11  A builders, two groups of four (one warp per TMEM sub-partition in
 //         each) taking alternate taps: thread = tile row; per tap it reads its
 //         row's 128-byte source row from the staging buffer and stores it as
@@ -265,8 +264,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
     uint8_t* lid_s = b_smem + (size_t)S * B_BYTES;                       // [NS][128 * K] uint16
     const int LID_BYTES = 128 * K * 2;
     int32_t* ulist = reinterpret_cast<int32_t*>(lid_s + NS * LID_BYTES);   // [2][TS_UMAX] source-row lists
-    uint8_t* epi_s = reinterpret_cast<uint8_t*>(ulist + 2 * TS_UMAX);      // [4][8][64 B] output transpose
-    uint64_t* bars = reinterpret_cast<uint64_t*>(epi_s + 4 * 8 * 64);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ulist + 2 * TS_UMAX);
     uint64_t* stg_full = bars;            // [2]
     uint64_t* stg_empty = bars + 2;       // [2]
     uint64_t* a_full = bars + 4;              // [TS_NA_MAX]
@@ -517,16 +515,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         }
     } else if (warp < 4) {
         // ====================================================== epilogue
-        // Thread = tile row for the TMEM loads.  Each 32-column chunk (64 bytes of a row) then
-        // goes out eight rows at a time through a 512-byte per-warp transpose buffer, so that
-        // every global store instruction writes eight whole 64-byte row segments.  Chunk u of
-        // buffer row r sits at r*64 + (u ^ (r >> 1)) * 16: the eight writers of a chunk and the
-        // readers (two rows x four chunks per 8-lane phase) are both free of bank conflicts.
-        // No bulk/TMA stores: the TMA unit carries the weight tiles, whose latency the MMA
-        // waits on.
-        uint8_t* es = epi_s + warp * 8 * 64;
-        const int wr = lane & 7;                  // this lane's row within its round of eight
-        const int rr = lane >> 2, uu = lane & 3;  // read-back: buffer row rr, 16-byte chunk uu
+        // Thread = tile row: each 32-column TMEM load becomes four 16-byte global stores of
+        // the row.  (Measured: routing the stores through a shared-memory transpose so that
+        // every store instruction writes whole 64-byte row segments made the drain slower,
+        // 2,989 -> 4,053 cycles a 64-column tile.)  No bulk/TMA stores: the TMA unit carries
+        // the weight tiles, whose latency the MMA waits on.  The accumulator is released
+        // once its last columns are in registers.
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
@@ -536,12 +530,13 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             tc_fence_after();
             const int64_t rt = t / p.grid_y;
             const int n0 = (int)(t % p.grid_y) * p.tile_n;
-            const int64_t row0 = rt * 128 + warp * 32;
+            const int64_t row = rt * 128 + tid;
             const uint32_t lane_addr = tmem_base + (uint32_t)(b * p.tile_n) + ((uint32_t)(warp * 32) << 16);
+            uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + (row < p.n_rows ? row : 0) * (int64_t)p.cout + n0);
             for (int c = 0; c < p.tile_n; c += 32) {
                 float v[32];
                 tmem_ld32(lane_addr + c, v);
-                if (c + 32 >= p.tile_n) {  // the accumulator is free once its last columns are in registers
+                if (c + 32 >= p.tile_n) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tmem_empty[b]);
@@ -551,18 +546,9 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 #pragma unroll
                     for (int e = 0; e < 32; ++e) v[e] = silu_bf16out(v[e]);
                 }
+                if (row < p.n_rows) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if ((lane >> 3) == j) {
-#pragma unroll
-                        for (int qq = 0; qq < 4; ++qq)
-                            cvt_store_bf16x8(es + wr * 64 + ((qq ^ (wr >> 1)) << 4), v + 8 * qq);
-                    }
-                    __syncwarp();
-                    const uint4 d = *reinterpret_cast<const uint4*>(es + rr * 64 + ((uu ^ (rr >> 1)) << 4));
-                    const int64_t row = row0 + j * 8 + rr;
-                    if (row < p.n_rows) *reinterpret_cast<uint4*>(p.out + row * (int64_t)p.cout + n0 + c + uu * 8) = d;
-                    __syncwarp();
+                    for (int qq = 0; qq < 4; ++qq) cvt_store_bf16x8(dst + (c + 8 * qq) * 2, v + 8 * qq);
                 }
             }
         }
@@ -579,7 +565,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 // Dynamic shared memory of a launch (1 KB alignment slack included).
 inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int n_stg) {
     return 1024 + (size_t)n_stg * u_cap * 128 + (size_t)b_stages * tile_n * 128 + (size_t)n_stg * 128 * K * 2 +
-           2 * TS_UMAX * 4 + 4 * 8 * 64 + (size_t)(4 + 2 * TS_NA_MAX + 2 * b_stages + 4) * 8 + 16;
+           2 * TS_UMAX * 4 + (size_t)(4 + 2 * TS_NA_MAX + 2 * b_stages + 4) * 8 + 16;
 }
 
 }  // namespace sc
