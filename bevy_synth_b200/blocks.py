@@ -151,19 +151,23 @@ class C2SUpsampleBlock:
                 raise F.SparseConvError(F._lib.SC_ERR_INVALID,
                                         "decoder stage requires guide_subdivisions but none were provided")
             _, mask = F.subdivision_head(x, p.w_sub, p.b_sub, threshold, return_logits=False)
+        # the child count stays on the device until conv1 is enqueued: conv1 writes each kept
+        # child's row through child_row and is sized by the 8 * Np bound, so the host reads the
+        # count only once the GPU has the parents' LayerNorm, map, schedule and conv1 queued
+        child_row, coords_bound, skip_bound, count = F.subdivide_async(coords, mask, self.cin)
         h = F.layer_norm_affine_silu_forward(x, p.ln1_g, p.ln1_b, C2S_LN_EPS)
-        child_row, child_coords, skip_off = F.subdivide(coords, mask, self.cin)
-        n_child = child_coords.shape[0]
         if nbr_parent is None:
             nbr_parent = F.neighbor_rows_tensor_from_coords_tensor(self.cfg1, coords)
         # parents grouped by their kept-children mask, then by tap mask: a tile whose
         # parents keep none of a child block skips that block's MMAs (dry stage)
         sched1 = F.neighbor_schedule(self.cfg1, nbr_parent, group_mask=mask) if self.group_children else None
-        h_up = F.sparse_subm_conv_forward(
+        h_up_bound = F.sparse_subm_conv_forward(
             self.cfg1, h, nbr_parent, p.w1, p.b1,
             F.Epilogue(layer_norm=True, ln_width=self.cout, ln_eps=C2S_LN_EPS, silu=True,
                        out_row_map=child_row, out_row_map_cols=8, schedule=sched1),
-            out_rows=n_child)
+            out_rows=coords_bound.shape[0])
+        n_child = count.value()
+        child_coords, skip_off, h_up = coords_bound[:n_child], skip_bound[:n_child], h_up_bound[:n_child]
         nbr_child = F.neighbor_rows_tensor_from_coords_tensor(self.cfg2, child_coords)
         # the child grid is sparse (config 3: ~7 of 27 taps per row): grouping rows by tap mask
         # halves the executed MMA work of conv2 and of the ResBlock convs that follow

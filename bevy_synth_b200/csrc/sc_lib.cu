@@ -1124,19 +1124,21 @@ int sc_subdiv_head(sc_dtype dtype, const void* feats, int64_t n, int64_t channel
     return SC_OK;
 }
 
-int sc_subdivide(const int32_t* parent_coords, const uint8_t* mask, int64_t n_parent,
-                 int64_t parent_channels, void* scratch, int32_t* child_row, int32_t* child_coords,
-                 int64_t* skip_offset, int64_t* h_children, void* stream) {
-    if (n_parent < 0 || !h_children) return fail(SC_ERR_INVALID, "invalid subdivide arguments");
+int sc_subdivide_async(const int32_t* parent_coords, const uint8_t* mask, int64_t n_parent,
+                       int64_t parent_channels, void* scratch, int32_t* child_row, int32_t* child_coords,
+                       int64_t* skip_offset, int32_t* d_children, void* stream) {
+    if (n_parent < 0 || !d_children) return fail(SC_ERR_INVALID, "invalid subdivide arguments");
     if (n_parent * 8 > 0x7fffffffLL) return fail(SC_ERR_UNSUPPORTED, "too many parents for int32 child rows");
-    *h_children = 0;
-    if (n_parent == 0) return SC_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (n_parent == 0) {
+        SC_CUDA_TRY(cudaMemsetAsync(d_children, 0, 4, st));
+        return SC_OK;
+    }
     if (!parent_coords || !mask || !scratch || !child_row)
         return fail(SC_ERR_INVALID, "null pointer");
     if (parent_channels % 8 != 0) return fail(SC_ERR_INVALID, "channel2spatial: in_channels is not divisible by 8");
     if ((reinterpret_cast<uintptr_t>(mask) & 7u) != 0 || !aligned16(parent_coords) || !aligned16(child_coords))
         return fail(SC_ERR_INVALID, "mask must be 8-byte and coordinates 16-byte aligned");
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t a = ((size_t)(n_parent + 1) * 4 + 255) / 256 * 256;
     int32_t* counts = static_cast<int32_t*>(scratch);
     int32_t* offsets = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + a);
@@ -1145,12 +1147,31 @@ int sc_subdivide(const int32_t* parent_coords, const uint8_t* mask, int64_t n_pa
     subdiv_count_kernel<<<grid1d(n_parent + 1, 256), 256, 0, st>>>(mask, n_parent, counts);
     SC_CUDA_TRY(cudaGetLastError());
     SC_CUDA_TRY(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, counts, offsets, (int)(n_parent + 1), st));
+    SC_CUDA_TRY(cudaMemcpyAsync(d_children, offsets + n_parent, 4, cudaMemcpyDeviceToDevice, st));
     subdiv_write_kernel<<<grid1d(n_parent, 256), 256, 0, st>>>(
         reinterpret_cast<const int4*>(parent_coords), mask, n_parent, parent_channels, offsets, child_row,
         reinterpret_cast<int4*>(child_coords), skip_offset);
     SC_CUDA_TRY(cudaGetLastError());
+    return SC_OK;
+}
+
+int sc_subdivide(const int32_t* parent_coords, const uint8_t* mask, int64_t n_parent,
+                 int64_t parent_channels, void* scratch, int32_t* child_row, int32_t* child_coords,
+                 int64_t* skip_offset, int64_t* h_children, void* stream) {
+    if (n_parent < 0 || !h_children) return fail(SC_ERR_INVALID, "invalid subdivide arguments");
+    *h_children = 0;
+    if (n_parent == 0) return SC_OK;
+    if (!scratch) return fail(SC_ERR_INVALID, "null pointer");
+    // the count goes to the scratch's spare tail (sc_subdivide_scratch_bytes leaves 256 bytes)
+    size_t bytes = 0;
+    sc_subdivide_scratch_bytes(n_parent, &bytes);
+    int32_t* d_count = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(scratch) + (bytes - 256 + 15) / 16 * 16);
+    if (int rc = sc_subdivide_async(parent_coords, mask, n_parent, parent_channels, scratch, child_row,
+                                    child_coords, skip_offset, d_count, stream))
+        return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
     int32_t total = 0;
-    SC_CUDA_TRY(cudaMemcpyAsync(&total, offsets + n_parent, 4, cudaMemcpyDeviceToHost, st));
+    SC_CUDA_TRY(cudaMemcpyAsync(&total, d_count, 4, cudaMemcpyDeviceToHost, st));
     SC_CUDA_TRY(cudaStreamSynchronize(st));
     *h_children = total;
     return SC_OK;

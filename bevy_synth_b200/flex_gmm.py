@@ -522,6 +522,46 @@ def subdivide(parent_coords: torch.Tensor, mask: torch.Tensor, parent_channels: 
     return child_row, coords[:k].contiguous(), skip[:k].contiguous()
 
 
+class DeviceCount:
+    """A row count left on the device by an asynchronous call: copied to pinned
+    host memory behind the producing kernels; ``value()`` waits for that copy
+    only (an event), not for the stream."""
+
+    def __init__(self, d_count: torch.Tensor):
+        self.host = torch.empty(1, dtype=d_count.dtype, pin_memory=True)
+        self.host.copy_(d_count, non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record(torch.cuda.current_stream(d_count.device))
+        self._value = None
+
+    def value(self) -> int:
+        if self._value is None:
+            self.event.synchronize()
+            self._value = int(self.host[0])
+        return self._value
+
+
+def subdivide_async(parent_coords: torch.Tensor, mask: torch.Tensor, parent_channels: int):
+    """sc_subdivide_async: like ``subdivide`` with the child count left on the
+    device.  Returns (child_row [Np, 8], child_coords [8 Np, 4], skip_offset
+    [8 Np], count: DeviceCount); rows >= count.value() of the last two are
+    unused."""
+    _coords_tensor(parent_coords)
+    _require_cuda("mask", mask)
+    n = parent_coords.shape[0]
+    dev = parent_coords.device
+    b = ctypes.c_size_t(0)
+    check(lib().sc_subdivide_scratch_bytes(n, ctypes.byref(b)))
+    scratch = torch.empty(max(b.value, 1), dtype=torch.uint8, device=dev)
+    child_row = torch.empty((n, 8), dtype=torch.int32, device=dev)
+    coords = torch.empty((max(8 * n, 1), 4), dtype=torch.int32, device=dev)
+    skip = torch.empty(max(8 * n, 1), dtype=torch.int64, device=dev)
+    d_count = torch.empty(4, dtype=torch.int32, device=dev)
+    check(lib().sc_subdivide_async(_ptr(parent_coords), _ptr(mask), n, parent_channels, _ptr(scratch),
+                                   _ptr(child_row), _ptr(coords), _ptr(skip), _ptr(d_count), _stream(parent_coords)))
+    return child_row, coords, skip, DeviceCount(d_count[:1])
+
+
 @dataclass(frozen=True)
 class SparsePatchify3dConfig:
     """Mirror of burn_flex_gmm's SparsePatchify3dConfig (src/lib.rs:26-35)."""

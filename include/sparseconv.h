@@ -255,6 +255,17 @@ int sc_subdivide(const int32_t* d_parent_coords, const uint8_t* d_mask, int64_t 
                  int64_t* d_skip_offset /* [<= 8*n_parent] */, int64_t* h_children,
                  void* stream);
 
+/* The same without the host read: the child count is written to d_children
+ * (one int32 on the device) and nothing synchronises.  A caller enqueues the
+ * work that needs no child count (the parents' LayerNorm, map and schedule,
+ * and conv1, whose outputs it sizes by the 8*n_parent bound) before it reads
+ * the count, so the GPU does not wait for the host at this point. */
+int sc_subdivide_async(const int32_t* d_parent_coords, const uint8_t* d_mask, int64_t n_parent,
+                       int64_t parent_channels, void* d_scratch, int32_t* d_child_row,
+                       int32_t* d_child_coords /* [8*n_parent, 4] */,
+                       int64_t* d_skip_offset /* [8*n_parent] */, int32_t* d_children,
+                       void* stream);
+
 /* ---- subdivision head (decoder upsample without a guide) -----------------
  * logits[n, 8] = feats[n, C] @ weight[8, C]^T + bias (the to_subdiv linear
  * layer; weight in feats' dtype, bias fp32, fp32 accumulate), optionally

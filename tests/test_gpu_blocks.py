@@ -51,6 +51,27 @@ def test_c2s_block(cuda_device, cin, cout):
     assert_no_fault()
 
 
+@pytest.mark.parametrize("n_keep", ["random", "none", "all"])
+def test_subdivide_async_matches_sync(cuda_device, n_keep):
+    """sc_subdivide_async leaves the child count on the device and writes the same child rows,
+    coordinates and skip offsets as sc_subdivide (which reads the count back)."""
+    coords = to_dev(shell(grid=24, r=8.0))
+    n = coords.shape[0]
+    mask = synth.child_mask(3, n)
+    if n_keep != "random":
+        mask[:] = 1 if n_keep == "all" else 0
+    m = to_dev(mask)
+    row_s, cc_s, sk_s = F.subdivide(coords, m, 64)
+    row_a, cc_a, sk_a, count = F.subdivide_async(coords, m, 64)
+    k = count.value()
+    assert k == cc_s.shape[0] == int(mask.sum())
+    assert cc_a.shape[0] == 8 * n
+    assert torch.equal(row_a, row_s)
+    assert torch.equal(cc_a[:k], cc_s)
+    assert torch.equal(sk_a[:k], sk_s)
+    assert_no_fault()
+
+
 def test_mini_upsample_pyramid(cuda_device):
     """Config-3 structure at reduced width/size: 12^3 grid, 256->128->64->32."""
     rng = np.random.default_rng(0)
