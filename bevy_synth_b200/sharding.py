@@ -239,12 +239,13 @@ class HaloPlan:
 class ShardedSubmStack:
     """SubM layer stack on a Morton-range-sharded grid.  Every row a peer reads
     is a boundary row, so a layer runs its boundary rows' conv first; the next
-    layer's halo exchange (pack + all-to-all, second stream) then overlaps this
-    layer's interior rows' conv, and the next layer's boundary conv starts as
-    soon as both are done.  Only the first layer's exchange (the input rows)
-    is exposed.  The interior conv is released once the pack has run, so the
-    all-to-all is already in flight when the conv's CTAs occupy the SMs.
-    Input and output rows are in Morton-local order."""
+    layer's halo exchange (pack + all-to-all, second stream) then runs beside
+    this layer's interior rows' conv, and the next layer's boundary conv starts
+    once both are done.  Only the first layer's exchange (the input rows) has
+    nothing to overlap.  Host order per layer: boundary conv, pack, interior
+    conv (released once the pack has run), all-to-all -- the host's time inside
+    the collective call passes while the interior conv runs.  Input and output
+    rows are in Morton-local order."""
 
     def __init__(self, stack, plan: HaloPlan, schedule: bool = True, _scheds=None, tile_sources: bool = True):
         from . import flex_gmm as F
@@ -293,9 +294,9 @@ class ShardedSubmStack:
         compute = torch.cuda.current_stream(dev)
         F.gather_rows(x_local, plan.order, out=self.bufs[0][:n])
 
-        def exchange(buf):
-            """Pack + all-to-all of ``buf``'s boundary rows on the comm stream, after the
-            compute stream's work so far; returns the (packed, halo arrived) events."""
+        def pack(buf):
+            """Packs ``buf``'s rows for the peers on the comm stream, after the compute
+            stream's work so far; returns (send rows, packed event)."""
             ready = torch.cuda.Event()
             ready.record(compute)
             with torch.cuda.stream(self.comm):
@@ -303,36 +304,45 @@ class ShardedSubmStack:
                 send = plan.pack(buf)
                 packed = torch.cuda.Event()
                 packed.record(self.comm)
+            return send, packed
+
+        def all_to_all(buf, send):
+            """The all-to-all of packed rows into ``buf``'s halo, on the comm stream;
+            returns the event of the halo's arrival."""
+            with torch.cuda.stream(self.comm):
                 plan.exchange(buf, send=send)
                 arrived = torch.cuda.Event()
                 arrived.record(self.comm)
-            return packed, arrived
+            return arrived
 
         layers = list(zip(self.stack.cfgs, self.stack.w, self.stack.b))
-        _, halo = exchange(self.bufs[0])
+        halo = all_to_all(self.bufs[0], pack(self.bufs[0])[0])
         for i, (cfg, w, b) in enumerate(layers):
             buf = self.bufs[i]
             last = i + 1 == len(layers)
             dst = self.out if last else self.bufs[i + 1][:n]
-            packed = None
+            send = None
             for rows, nbr, sched, ts, order, boundary in (
                     (slice(ni, n), self.nbr_bnd, self.sched_bnd, self.ts_bnd, self.order_bnd, True),
                     (slice(0, ni), self.nbr_int, self.sched_int, self.ts_int, self.order_int, False)):
                 if boundary:
                     compute.wait_event(halo)
                 elif not last:
-                    # the next layer's halo: its rows are this layer's boundary outputs
-                    packed, halo = exchange(self.bufs[i + 1])
+                    # the next layer's halo rows are this layer's boundary outputs: pack them before
+                    # the interior conv takes the SMs; the all-to-all is enqueued after the conv, so
+                    # the host's time in the collective call is spent while the conv runs
+                    send, packed = pack(self.bufs[i + 1])
                     compute.wait_event(packed)
-                if rows.stop <= rows.start:
-                    continue
-                if last:  # rows go straight to their Morton-local place
-                    F.sparse_subm_conv_forward(cfg, buf, nbr, w, b, F.Epilogue(
-                        silu=self.stack.silu, schedule=sched, out_row_map=order, out_row_map_cols=1),
-                        out=dst, out_rows=n)
-                else:
-                    from .blocks import layer_epilogue
+                if rows.stop > rows.start:
+                    if last:  # rows go straight to their Morton-local place
+                        F.sparse_subm_conv_forward(cfg, buf, nbr, w, b, F.Epilogue(
+                            silu=self.stack.silu, schedule=sched, out_row_map=order, out_row_map_cols=1),
+                            out=dst, out_rows=n)
+                    else:
+                        from .blocks import layer_epilogue
 
-                    F.sparse_subm_conv_forward(cfg, buf, nbr, w, b, layer_epilogue(cfg, self.stack.silu, sched, ts),
-                                               out=dst[rows])
+                        F.sparse_subm_conv_forward(cfg, buf, nbr, w, b,
+                                                   layer_epilogue(cfg, self.stack.silu, sched, ts), out=dst[rows])
+            if send is not None:
+                halo = all_to_all(self.bufs[i + 1], send)
         return self.out
