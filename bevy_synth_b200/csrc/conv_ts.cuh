@@ -49,6 +49,7 @@ constexpr int TS_NA_MAX = 12;     // A slots in TMEM (32 columns each) at most
 constexpr int TS_THREADS = 18 * 32;
 constexpr int TS_EPI0 = 0, TS_BLD0 = 4, TS_STG0 = 12, TS_BLOADER = 16, TS_MMA = 17;
 constexpr uint16_t TS_NONE = 0xFFFF;
+constexpr int TS_EPI_BYTES = 4 * 32 * 128;  // TMA epilogue staging: one 32-row x 64-column bf16 box per warp
 
 // ---- prepass: per-tile distinct source rows -----------------------------------
 // Layout of the tile-source plan (one buffer):
@@ -226,6 +227,7 @@ struct TsParams {
     int grp;         // taps per pipeline step (G): 4 for tile_n <= 64, else 2
     int n_a;         // A slots (a multiple of grp, <= TS_NA_MAX)
     int a_col0;      // first TMEM column of the A slots (n_buf * tile_n)
+    int tma_epi;     // 1: outputs by TMA tile stores of 32 rows x 64 columns (omap), tile_n % 64 == 0
 };
 
 // Named barrier 1 over the four staging warps (128 threads).
@@ -251,6 +253,7 @@ __device__ __forceinline__ uint32_t ts_mask_of(const TsParams& p, int64_t row_ti
 }
 
 __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_constant__ CUtensorMap wmap,
+                                                                 const __grid_constant__ CUtensorMap omap,
                                                                  const TsParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -264,7 +267,10 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
     uint8_t* lid_s = b_smem + (size_t)S * B_BYTES;                       // [NS][128 * K] uint16
     const int LID_BYTES = 128 * K * 2;
     int32_t* ulist = reinterpret_cast<int32_t*>(lid_s + NS * LID_BYTES);   // [2][TS_UMAX] source-row lists
-    uint64_t* bars = reinterpret_cast<uint64_t*>(ulist + 2 * TS_UMAX);
+    // [4][32 rows][128 B] TMA epilogue staging (1024-aligned: the 128-byte swizzle of the output map)
+    uint8_t* epi_s = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(ulist + 2 * TS_UMAX) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(p.tma_epi ? epi_s + TS_EPI_BYTES : (uint8_t*)(ulist + 2 * TS_UMAX));
     uint64_t* stg_full = bars;            // [2]
     uint64_t* stg_empty = bars + 2;       // [2]
     uint64_t* a_full = bars + 4;              // [TS_NA_MAX]
@@ -515,12 +521,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
         }
     } else if (warp < 4) {
         // ====================================================== epilogue
-        // Thread = tile row: each 32-column TMEM load becomes four 16-byte global stores of
-        // the row.  (Measured: routing the stores through a shared-memory transpose so that
-        // every store instruction writes whole 64-byte row segments made the drain slower,
-        // 2,989 -> 4,053 cycles a 64-column tile.)  No bulk/TMA stores: the TMA unit carries
-        // the weight tiles, whose latency the MMA waits on.  The accumulator is released
-        // once its last columns are in registers.
+        // Thread = tile row.  Plain mode: each 32-column TMEM load becomes four 16-byte global
+        // stores of the row.  (Measured: routing the stores through a shared-memory transpose so
+        // that every store instruction writes whole 64-byte row segments made the drain slower,
+        // 2,989 -> 4,053 cycles a 64-column tile.)  TMA mode (tma_epi, the single-buffered wide
+        // accumulator, whose drain the MMAs wait for): 64 columns at a time, the warp writes its
+        // 32 rows into a 128B-swizzled 4 KB box and one lane stores the box with a tiled TMA
+        // store; the next box waits until that store has read the staging.  The accumulator is
+        // released once its last columns are in registers.
+        uint8_t* es = epi_s + warp * 32 * 128;
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
@@ -532,6 +541,37 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
             const int n0 = (int)(t % p.grid_y) * p.tile_n;
             const int64_t row = rt * 128 + tid;
             const uint32_t lane_addr = tmem_base + (uint32_t)(b * p.tile_n) + ((uint32_t)(warp * 32) << 16);
+            if (p.tma_epi) {
+                for (int c = 0; c < p.tile_n; c += 64) {
+                    if (lane == 0) bulk_wait_read_all();  // the previous box's store has read the staging
+                    __syncwarp();
+#pragma unroll 1
+                    for (int h = 0; h < 2; ++h) {  // 32 columns at a time: chunks 4h .. 4h + 3 of the box rows
+                        float v[32];
+                        tmem_ld32(lane_addr + c + 32 * h, v);
+                        if (c + 32 * h + 32 >= p.tile_n) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&tmem_empty[b]);
+                        }
+                        if (p.bias) add_param32(v, p.bias + n0 + c + 32 * h, false);
+                        if (p.silu) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) v[e] = silu_bf16out(v[e]);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            cvt_store_bf16x8(es + lane * 128 + (((4 * h + u) ^ (lane & 7)) << 4), v + 8 * u);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&omap, smem_u32(es), n0 + c, (int)(rt * 128 + warp * 32));
+                        bulk_commit();
+                    }
+                }
+                continue;
+            }
             uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + (row < p.n_rows ? row : 0) * (int64_t)p.cout + n0);
             for (int c = 0; c < p.tile_n; c += 32) {
                 float v[32];
@@ -552,6 +592,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
                 }
             }
         }
+        if (p.tma_epi && lane == 0) bulk_wait_all();  // every output box written before the CTA leaves
     }
 
     tc_fence_before();
@@ -563,9 +604,9 @@ __global__ void __launch_bounds__(TS_THREADS, 1) conv_ts_kernel(const __grid_con
 }
 
 // Dynamic shared memory of a launch (1 KB alignment slack included).
-inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int n_stg) {
+inline size_t ts_smem_bytes(int u_cap, int tile_n, int K, int b_stages, int n_stg, bool tma_epi = false) {
     return 1024 + (size_t)n_stg * u_cap * 128 + (size_t)b_stages * tile_n * 128 + (size_t)n_stg * 128 * K * 2 +
-           2 * TS_UMAX * 4 + (size_t)(4 + 2 * TS_NA_MAX + 2 * b_stages + 4) * 8 + 16;
+           2 * TS_UMAX * 4 + (tma_epi ? 1024 + TS_EPI_BYTES : 0) + (size_t)(4 + 2 * TS_NA_MAX + 2 * b_stages + 4) * 8 + 16;
 }
 
 }  // namespace sc

@@ -327,6 +327,15 @@ __device__ __forceinline__ void tma_scatter4(const void* desc, uint32_t src, int
         : "memory");
 }
 
+// Tiled 2-D store: the box at src (the map's swizzle applied) -> columns x.., rows y.. of
+// the tensor; rows past the tensor's end are not written.  Tracked by this thread's bulk
+// groups.  x * element size must be a multiple of 16 bytes and y >= 0.
+__device__ __forceinline__ void tma_store_2d(const void* desc, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(desc), "r"(x),
+                 "r"(y), "r"(src)
+                 : "memory");
+}
+
 // ------------------------------------------------ 1-D bulk copies (TMA) --
 // shared -> global, tracked by this thread's bulk groups (no mbarrier).
 __device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {

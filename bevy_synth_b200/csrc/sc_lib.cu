@@ -418,7 +418,7 @@ static int launch_tc(const sc_conv_config* c, const void* in, int64_t n_in, cons
 // The tile-source (A-from-TMEM) kernel: bf16, 64 input channels, <= 128 outputs, a plain bias/SiLU
 // epilogue, map rows in order, and a usable tile-source plan.  SC_TS=0 turns it off.
 struct TsPlan {
-    int tile_n, grid_y, u_cap, stages, n_buf, n_stg, grp, n_a, a_col0;
+    int tile_n, grid_y, u_cap, stages, n_buf, n_stg, grp, n_a, a_col0, tma_epi;
     size_t smem;
 };
 
@@ -432,8 +432,10 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     if (e.tile_sources_max < 0 || e.tile_sources_max > TS_UMAX) return false;
     // One column tile of at most 128 outputs, accumulators double-buffered (the epilogue of one
     // tile overlaps the next tile's MMAs).  Wider outputs stay on the generic kernel: measured on
-    // config 5's 64->256 layer, one 256-wide single-buffered accumulator (6.3 ms) and two 128-wide
-    // column tiles that stage and build A twice (7.8 ms) both lost to it (5.8 ms).
+    // config 5's 64->256 layer (isolated, max clock), one 256-wide single-buffered accumulator
+    // (6.26 ms with per-row stores, 5.82 ms with TMA box stores) and two 128-wide column tiles that
+    // stage and build A twice (7.8 ms) all lost to it (4.74 ms): in map order a tile executes all
+    // 27 taps, against 17.9 on the conv schedule.
     // SC_TS_WIDE=1 (one single-buffered accumulator up to 256 wide) and SC_TS_WIDE=2 (128-wide
     // column tiles, each staging and building A again) opt wider outputs in.
     const char* wide_env = std::getenv("SC_TS_WIDE");
@@ -455,15 +457,19 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     plan->a_col0 = plan->n_buf * tile_n;
     plan->n_a = std::min(TS_NA_MAX, ((int)TC_TMEM_COLS - plan->a_col0) / 32) / plan->grp * plan->grp;
     if (plan->n_a < 2 * plan->grp) return false;
+    // outputs by TMA box stores for the single-buffered accumulator, whose drain the MMAs wait
+    // for (SC_TS_TMAEPI=0|1 pins it)
+    const char* te_env = std::getenv("SC_TS_TMAEPI");
+    plan->tma_epi = (te_env ? te_env[0] == '1' : plan->n_buf == 1) && tile_n % 64 == 0 ? 1 : 0;
     // double-buffered staging with >= 3 weight stages if it fits, else single-buffered staging
     for (int ns = 2; ns >= 1; --ns) {
         int S = 12;
-        while (S >= 2 && ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, ns) > kMaxDynSmem) --S;
+        while (S >= 2 && ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, ns, plan->tma_epi) > kMaxDynSmem) --S;
         S = S / plan->grp * plan->grp;  // whole slot groups
         if (S >= 2 * plan->grp) {
             plan->stages = S;
             plan->n_stg = ns;
-            plan->smem = ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, ns);
+            plan->smem = ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, ns, plan->tma_epi);
             return true;
         }
     }
@@ -511,6 +517,19 @@ static int launch_ts(const sc_conv_config* c, const void* in, int64_t n_in, int6
     p.grp = plan.grp;
     p.n_a = plan.n_a;
     p.a_col0 = plan.a_col0;
+    p.tma_epi = plan.tma_epi;
+    CUtensorMap omap;
+    memset(&omap, 0, sizeof omap);
+    if (plan.tma_epi) {
+        cuuint64_t od[2] = {(cuuint64_t)cout, (cuuint64_t)n_rows};
+        cuuint64_t os[1] = {(cuuint64_t)cout * 2};
+        cuuint32_t ob[2] = {64u, 32u};
+        cuuint32_t oe[2] = {1u, 1u};
+        CUresult ro = enc(&omap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, od, os, ob, oe, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (ro != CUDA_SUCCESS)
+            return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed with code " + std::to_string((int)ro));
+    }
     static std::once_flag ts_once;
     static cudaError_t ts_err = cudaSuccess;
     std::call_once(ts_once, [] {
@@ -519,7 +538,7 @@ static int launch_ts(const sc_conv_config* c, const void* in, int64_t n_in, int6
     });
     SC_CUDA_TRY(ts_err);
     const int64_t ctas = std::min<int64_t>(p.n_tiles, sm_count());
-    conv_ts_kernel<<<(unsigned)ctas, TS_THREADS, plan.smem, st>>>(wmap, p);
+    conv_ts_kernel<<<(unsigned)ctas, TS_THREADS, plan.smem, st>>>(wmap, omap, p);
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
 }
