@@ -367,13 +367,87 @@ __global__ void __launch_bounds__(F32_THREADS) conv_f32_tiled_kernel(
 // map is null; skipped when negative).  Two-pass statistics as the reference
 // (burn_trellis sparse_decoder_wgpu_ops.rs:1642-1711): mean, then biased
 // variance sum((x-mean)^2)/C, inv_std = 1/sqrt(var + eps).
+// rpw = 0: one warp per entry, scalar loads (any dtype, width, alignment).  rpw in
+// {1, 2, 4, 8, 16, 32} (bf16 only; width % 8 == 0, width <= 1024, ld % 8 == 0, x and y
+// 16-byte aligned; rows_norm_act_rpw decides, and takes it for width <= 128): rpw entries per warp, a group of
+// 32 / rpw lanes per entry, each lane holding up to four 16-byte chunks of 8 values in
+// registers, so a row is read from memory once and narrow rows keep every lane busy.
 template <typename T>
 __global__ void __launch_bounds__(256) rows_norm_act_kernel(
     const T* __restrict__ x, T* __restrict__ y, int64_t n_entries, int width, int64_t ld,
     const int32_t* __restrict__ row_map, const float* __restrict__ gamma,
-    const float* __restrict__ beta, float eps, int do_ln, int do_silu) {
+    const float* __restrict__ beta, float eps, int do_ln, int do_silu, int rpw) {
     const int lane = threadIdx.x & 31;
-    int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t warp_id = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (rpw > 0) {
+        const int G = 32 / rpw;                 // lanes per entry
+        const int sub = lane & (G - 1);
+        const int64_t e = warp_id * rpw + lane / G;
+        const bool live = e < n_entries;
+        const int64_t row = live ? (row_map ? (int64_t)row_map[e] : e) : -1;
+        const int w8 = width >> 3;
+        uint4 u[4];
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c8 = sub + G * j;
+            if (row >= 0 && c8 < w8) {
+                u[j] = __ldg(reinterpret_cast<const uint4*>(x + row * ld) + c8);
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 f = __bfloat1622float2(h[q]);
+                    s += f.x + f.y;
+                }
+            }
+        }
+        float mean = 0.f, rstd = 1.f;
+        if (do_ln) {
+            for (int o = G >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            mean = s / (float)width;
+            float v = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (row >= 0 && sub + G * j < w8) {
+                    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float2 f = __bfloat1622float2(h[q]);
+                        v += (f.x - mean) * (f.x - mean) + (f.y - mean) * (f.y - mean);
+                    }
+                }
+            }
+            for (int o = G >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            rstd = 1.0f / sqrtf(v / (float)width + eps);
+        }
+        if (row < 0) return;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c8 = sub + G * j;
+            if (c8 < w8) {
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+                uint4 o4;
+                __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o4);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float2 f = __bfloat1622float2(h[q]);
+                    float a0 = f.x, a1 = f.y;
+                    const int c = 8 * c8 + 2 * q;
+                    if (do_ln) {
+                        a0 = (a0 - mean) * rstd;
+                        a1 = (a1 - mean) * rstd;
+                        if (gamma) { a0 *= gamma[c]; a1 *= gamma[c + 1]; }
+                        if (beta) { a0 += beta[c]; a1 += beta[c + 1]; }
+                    }
+                    if (do_silu) { a0 = silu_f(a0); a1 = silu_f(a1); }
+                    oh[q] = __floats2bfloat162_rn(a0, a1);
+                }
+                reinterpret_cast<uint4*>(y + row * ld)[c8] = o4;
+            }
+        }
+        return;
+    }
+    const int64_t e = warp_id;
     if (e >= n_entries) return;
     int64_t row = row_map ? (int64_t)row_map[e] : e;
     if (row < 0) return;
@@ -405,6 +479,21 @@ __global__ void __launch_bounds__(256) rows_norm_act_kernel(
         if (do_silu) a = silu_f(a);
         yr[c] = from_f32<T>(a);
     }
+}
+
+// Entries per warp of rows_norm_act_kernel's vector path for these arguments, or 0 for the
+// scalar path: one lane group of the smallest power of two >= width / 8 lanes per entry.
+// Taken for rows of at most 128 values (two or more rows per warp).  Measured on B200 against
+// the scalar path: 1M x 64 326 -> 150 us, 420k x 96 168 -> 131 us; wider rows were slower
+// (105k x 192 59 -> 78 us, 102k x 256 50 -> 82 us).
+template <typename T>
+inline int rows_norm_act_rpw(const void* x, const void* y, int64_t width, int64_t ld) {
+    if (sizeof(T) != 2 || width % 8 != 0 || width > 128 || ld % 8 != 0 ||
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) != 0)
+        return 0;
+    int g = 1;
+    while (g < 32 && g < width / 8) g <<= 1;
+    return 32 / g;
 }
 
 }  // namespace sc

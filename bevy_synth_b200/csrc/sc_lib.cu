@@ -595,9 +595,10 @@ static int launch_simt(const sc_conv_config* c, const void* in, int64_t n_in, co
             entries = n_rows * (cout / width);
         }
         T* dst = static_cast<T*>(e.d_out2 ? e.d_out2 : out);
-        rows_norm_act_kernel<T><<<grid1d(entries * 32, 256), 256, 0, st>>>(
+        const int rpw = rows_norm_act_rpw<T>(out, dst, width, ld);
+        rows_norm_act_kernel<T><<<grid1d((entries + (rpw ? rpw : 1) - 1) / (rpw ? rpw : 1) * 32, 256), 256, 0, st>>>(
             static_cast<const T*>(out), dst, entries, (int)width, ld, map, e.d_ln_gamma, e.d_ln_beta,
-            e.ln_eps, e.layer_norm, e.silu);
+            e.ln_eps, e.layer_norm, e.silu, rpw);
         SC_CUDA_TRY(cudaGetLastError());
     } else if (e.d_out2) {
         const size_t bytes = (size_t)(e.d_out_row_map ? 0 : n_rows * c->out_channels) * sizeof(T);
@@ -964,14 +965,17 @@ int sc_layer_norm_act(sc_dtype dtype, const void* x, int64_t rows, int64_t chann
     if (rows == 0) return SC_OK;
     if (!x || !y) return fail(SC_ERR_INVALID, "null pointer");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (dtype == SC_DTYPE_F32)
+    if (dtype == SC_DTYPE_F32) {
         rows_norm_act_kernel<float><<<grid1d(rows * 32, 256), 256, 0, st>>>(
             static_cast<const float*>(x), static_cast<float*>(y), rows, (int)channels, channels, nullptr,
-            gamma, beta, eps, ln, silu);
-    else
-        rows_norm_act_kernel<__nv_bfloat16><<<grid1d(rows * 32, 256), 256, 0, st>>>(
+            gamma, beta, eps, ln, silu, 0);
+    } else {
+        const int rpw = rows_norm_act_rpw<__nv_bfloat16>(x, y, channels, channels);
+        rows_norm_act_kernel<__nv_bfloat16><<<grid1d((rows + (rpw ? rpw : 1) - 1) / (rpw ? rpw : 1) * 32, 256), 256,
+                                               0, st>>>(
             static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), rows, (int)channels,
-            channels, nullptr, gamma, beta, eps, ln, silu);
+            channels, nullptr, gamma, beta, eps, ln, silu, rpw);
+    }
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
 }

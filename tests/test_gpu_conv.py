@@ -407,10 +407,15 @@ def test_pair_and_single_cta_kernels_agree(cuda_device, monkeypatch, cin, cout, 
 
 
 @pytest.mark.parametrize("channels,dtype", [(256, BF16), (512, BF16), (768, BF16), (1024, BF16), (96, BF16),
+                                            (8, BF16), (16, BF16), (64, BF16), (128, BF16), (192, BF16), (2048, BF16),
+                                            (100, BF16),
                                             (256, torch.float32)])
 def test_layer_norm_act_rows(cuda_device, channels, dtype):
     """LayerNorm(+affine) -> SiLU, LayerNorm alone and SiLU alone over rows (the row
-    kernel the decoder blocks run before their first conv), bf16 and fp32."""
+    kernel the decoder blocks run before their first conv), bf16 and fp32.  The bf16
+    widths cover the lane-group sizes of the vector path (8 .. 128 values: 32 to 2
+    rows per warp) and the scalar path (wider rows, and 100 values: not a multiple
+    of 8); 1000 rows leave a partly filled last warp."""
     rng = np.random.default_rng(channels)
     n = 1000
     x = (rng.standard_normal((n, channels)) * 2 + 0.5).astype(np.float32)
