@@ -117,14 +117,26 @@ __global__ void __launch_bounds__(256) nb_query_kernel(const int4* __restrict__ 
     out[idx] = found;
 }
 
-inline uint64_t nb_capacity(int64_t n_in) {
+// Table slots: the power of two >= 4 n_in (load factor <= 0.25: an absent key -- most taps
+// of a sparse grid -- ends its linear probe after ~1.4 slots on average, against ~2.5 at
+// 0.5), or, in a workspace too small for that, >= 2 n_in (load factor <= 0.5).
+inline uint64_t nb_capacity_min(int64_t n_in) {
     uint64_t cap = 1024;
     while (cap < (uint64_t)n_in * 2) cap <<= 1;
     return cap;
 }
 
+inline uint64_t nb_capacity(int64_t n_in) { return nb_capacity_min(n_in) * 2; }
+
 inline size_t nb_workspace_bytes(int64_t n_in) {
     return 256 + (size_t)nb_capacity(n_in) * sizeof(HashSlot);
+}
+
+// Capacity used with a workspace of ws_bytes (0 if it cannot hold the minimum table).
+inline uint64_t nb_capacity_for(int64_t n_in, size_t ws_bytes) {
+    if (ws_bytes >= nb_workspace_bytes(n_in)) return nb_capacity(n_in);
+    const uint64_t lo = nb_capacity_min(n_in);
+    return ws_bytes >= 256 + (size_t)lo * sizeof(HashSlot) ? lo : 0;
 }
 
 }  // namespace sc

@@ -697,7 +697,8 @@ int sc_neighbor_map_query(const sc_conv_config* cfg, const int32_t* in_coords, i
         return fail(SC_ERR_UNSUPPORTED, "neighbor map supports kernel extents up to 255");
     if (n_in < 0 || n_q < 0) return fail(SC_ERR_INVALID, "negative row count");
     if (n_in > 0x7ffffffeLL) return fail(SC_ERR_INVALID, "sparse conv coord row count exceeds i32::MAX");
-    if (!ws || ws_bytes < nb_workspace_bytes(n_in))
+    const uint64_t cap = nb_capacity_for(n_in, ws_bytes);
+    if (!ws || cap == 0)
         return fail(SC_ERR_CAPACITY, "neighbor workspace too small: need " +
                                          std::to_string(nb_workspace_bytes(n_in)) + " bytes");
     if ((n_in && !in_coords) || (n_q && (!q_coords || !out)))
@@ -705,7 +706,6 @@ int sc_neighbor_map_query(const sc_conv_config* cfg, const int32_t* in_coords, i
     if (!aligned16(in_coords) || !aligned16(q_coords) || !aligned16(ws))
         return fail(SC_ERR_INVALID, "coordinates and workspace must be 16-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const uint64_t cap = nb_capacity(n_in);
     NbStatus* status = static_cast<NbStatus*>(ws);
     HashSlot* table = reinterpret_cast<HashSlot*>(static_cast<uint8_t*>(ws) + 256);
     SC_CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(NbStatus), st));

@@ -130,7 +130,10 @@ int sc_kernel_offsets(const sc_conv_config* cfg, int32_t* h_offsets /* [K*3] */)
  * (same batch), or -1.  Duplicate coordinates resolve to the LOWEST row, as
  * every device builder of the reference does (src/wgpu/neighbor_kernels.rs:
  * 37-39, 249-256).  Coordinate components must lie in [0, 65534]; a violation
- * is recorded in the workspace status (SC_ERR_RANGE from sc_neighbor_status). */
+ * is recorded in the workspace status (SC_ERR_RANGE from sc_neighbor_status).
+ * sc_neighbor_workspace_bytes gives a table of >= 4 n_in slots (load factor
+ * <= 0.25); a workspace of at least 256 + 16 * (the power of two >= 2 n_in)
+ * bytes is accepted and runs at load factor <= 0.5. */
 int sc_neighbor_workspace_bytes(int64_t n_in, size_t* h_bytes);
 int sc_neighbor_map(const sc_conv_config* cfg, const int32_t* d_coords, int64_t n_rows,
                     void* d_workspace, size_t workspace_bytes, int32_t* d_neighbor_rows,

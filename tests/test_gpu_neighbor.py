@@ -111,3 +111,32 @@ def test_near_boundary_coordinates(cuda_device):
     coords = np.array([[0, 65534, 65534, 65534], [0, 65533, 65534, 65534], [7, 0, 0, 0], [7, 1, 0, 0]],
                       np.int32)
     check(F.SparseSubmConvConfig(4, 4), coords)
+
+
+def test_minimum_workspace_gives_the_same_map(cuda_device):
+    """A workspace of the minimum size (table of 2n slots, load factor 0.5) and the
+    full one (4n slots) give the same, oracle-exact map; one byte less than the
+    minimum is refused."""
+    import torch
+
+    from gpu_util import to_dev
+
+    coords = synth.config2(0, blocks=1, channels=8).coords
+    cfg = F.SparseSubmConvConfig(4, 4)
+    n = coords.shape[0]
+    ct = to_dev(coords)
+    full = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct)
+    cap = 1024
+    while cap < 2 * n:
+        cap <<= 1
+    ws = F.NeighborWorkspace(ct.device, n)
+    assert ws.bytes >= 256 + 2 * cap * 16
+    ws.bytes = 256 + cap * 16
+    small = F.neighbor_rows_tensor_from_coords_tensor(cfg, ct, workspace=ws)
+    assert torch.equal(small, full)
+    exp = oracle.build_neighbor_rows(ocfg(cfg), np.asarray(coords, np.uint32), oracle.DUP_LOWEST, None)
+    np.testing.assert_array_equal(full.cpu().numpy(), exp)
+    ws.bytes -= 1
+    with pytest.raises(F.SparseConvError):
+        F.neighbor_rows_tensor_from_coords_tensor(cfg, ct, workspace=ws)
+    assert_no_fault()
