@@ -298,7 +298,9 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
     uint64_t* pair_bar = mask_bar + 1;                     // PAIR: the peer CTA's tap mask arrived (single CTA:
                                                            // never arrived; the test stall mode waits on it)
     uint64_t* res_bar = pair_bar + 1;                      // [4] per epilogue warp: staged residual rows landed
-    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(res_bar + 4);  // [S] 2 = a tile's last step (bookkeeping, not read)
+    // [S] bit 1: a tile's last step (bookkeeping); bits 8+: the stage's 16-channel MMA steps
+    // when fewer than TC_BK / 16 (the last 64-channel chunk of a Cin % 64 != 0 conv), else 0
+    uint32_t* stage_flags = reinterpret_cast<uint32_t*>(res_bar + 4);
     uint32_t* tile_steps = stage_flags + S;  // [8] reduction steps per tile, ring over tiles
     // (the producers run at most S <= 8 stages, so at most 8 one-step tiles, ahead of the MMA thread)
     uint32_t* misc = tile_steps + 8;      // [0] tmem base, [1] abort
@@ -354,7 +356,8 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
         mbar_init(pair_bar, 1);
         for (int w = 0; w < 4; ++w) mbar_init(&res_bar[w], 1);  // lane 0's expect_tx arrive
         misc[1] = 0;
-        misc[2] = 0xffffffffu;  // PAIR peer: stages its producers issued, once they are done
+        misc[2] = 0xffffffffu;
+        for (int q = 0; q < S; ++q) stage_flags[q] = 0u;  // PAIR peer: stages its producers issued, once they are done
         fence_mbar_init();
         fence_proxy_async_smem();
     }
@@ -661,6 +664,8 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
                         const uint32_t bar = PAIR ? leader_full0 + (uint32_t)(s * 8) : smem_u32(&full[s]);
                         if (lane == 0 && pw == 0) {
                             if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
+                            const int tail16 = ch == n_chunks - 1 ? ((p.cin % TC_BK) + 15) / 16 : 0;
+                            stage_flags[s] = (step == n_steps - 1 ? 2u : 0u) | ((uint32_t)tail16 << 8);
                             if (!PAIR || leader)
                                 mbar_arrive_expect_tx(&full[s], (uint32_t)((PAIR ? 2 : 1) * (TC_A_BYTES + B_BYTES)));
                             const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
@@ -689,7 +694,8 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
                     if (b_lane) {
                         // published to the MMA thread by this stage's full-barrier arrive below
                         if (step == 0) tile_steps[lt & 7] = (uint32_t)n_steps;
-                        stage_flags[s] = step == n_steps - 1 ? 2u : 0u;
+                        const int tail16 = ch == n_chunks - 1 ? ((p.cin % TC_BK) + 15) / 16 : 0;
+                        stage_flags[s] = (step == n_steps - 1 ? 2u : 0u) | ((uint32_t)tail16 << 8);
                         const uint32_t dst = smem_u32(b_smem + s * B_BYTES);
                         if (!PAIR) {
                             mbar_arrive_expect_tx(&full[s], (uint32_t)(B_BYTES + (p.gather4 == 2 ? TC_A_BYTES / 2 : 0)));
@@ -808,9 +814,14 @@ __global__ void __launch_bounds__(tc_threads(TC_PW), 1)
                     if (step == 0) steps = tile_steps[lt & 7];
                     const uint64_t ad = adesc0 + (uint64_t)((s * TC_A_BYTES) >> 4);
                     const uint64_t bd = bdesc0 + (uint64_t)((s * B_BYTES) >> 4);
+                    // a 32-channel tail chunk (e.g. Cin = 96) runs 2 of the 4 MMAs: the rest of its
+                    // A and B rows are zero fill
+                    const uint32_t kn = stage_flags[s] >> 8;
+                    const int k16 = kn ? (int)kn : TC_BK / 16;
                     if (issuer) {
 #pragma unroll
                         for (int kk = 0; kk < TC_BK / 16; ++kk) {
+                            if (kk >= k16) break;
                             const uint32_t accum = (step == 0 && kk == 0) ? 0u : 1u;
                             // K step kk: +32 bytes inside the 128-byte swizzled rows
                             if (PAIR) {

@@ -131,8 +131,11 @@ def bf16_ref(cfg, x, w, b, nbr):
 
 
 @pytest.mark.parametrize("cin,cout", [(64, 64), (96, 96), (128, 256), (192, 192), (256, 256), (384, 384),
-                                      (512, 512), (768, 384), (64, 768), (256, 3072)])
+                                      (512, 512), (768, 384), (64, 768), (256, 3072),
+                                      (72, 128), (160, 96), (224, 64)])
 def test_bf16_tensor_core_widths(cuda_device, cin, cout):
+    """Widths on the tcgen05 kernel vs the oracle; Cin of 72, 96, 160, 224 end in a partial
+    64-channel chunk whose stage runs only the MMAs of its real channels."""
     coords = shell()
     rng = np.random.default_rng(cin * 7 + cout)
     x = rng.standard_normal((coords.shape[0], cin)).astype(np.float32)
