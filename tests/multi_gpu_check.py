@@ -83,7 +83,9 @@ def main():
     finally:
         dist.barrier()
         dist.destroy_process_group()
-    print(json.dumps(out), flush=True)
+    # one write of the whole line (<= PIPE_BUF bytes: atomic), so the ranks' lines do not interleave
+    sys.stdout.write(json.dumps(out) + "\n")
+    sys.stdout.flush()
     sys.exit(0 if out.get("ok") else 1)
 
 

@@ -14,6 +14,24 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
+def _json_objects(text: str) -> list:
+    """Every top-level JSON object in the ranks' merged output, also when two
+    ranks' lines ended up on one line."""
+    dec, objs, i = json.JSONDecoder(), [], 0
+    while True:
+        i = text.find("{", i)
+        if i < 0:
+            return objs
+        try:
+            obj, end = dec.raw_decode(text, i)
+        except json.JSONDecodeError:
+            i += 1
+            continue
+        if isinstance(obj, dict) and "ok" in obj:
+            objs.append(obj)
+        i = end
+
+
 def _port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -31,6 +49,6 @@ def test_sharding_matches_single_gpu(world):
            os.path.join(HERE, "multi_gpu_check.py")]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
-    lines = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
+    lines = _json_objects(r.stdout)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert len(lines) == world and all(l["ok"] for l in lines), lines
