@@ -453,6 +453,10 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     // taps per pipeline step: the per-step barrier work is paid once per G taps, which narrow
     // outputs (little tensor work per tap) need most
     plan->grp = tile_n <= 64 ? 4 : 2;
+    if (const char* g_env = std::getenv("SC_TS_G")) {  // tuning: taps per step (1, 2 or 4)
+        const int g = std::atoi(g_env);
+        if (g == 1 || g == 2 || g == 4) plan->grp = g;
+    }
     // A slots: the TMEM columns the two accumulators leave, whole slot groups of G
     plan->a_col0 = plan->n_buf * tile_n;
     plan->n_a = std::min(TS_NA_MAX, ((int)TC_TMEM_COLS - plan->a_col0) / 32) / plan->grp * plan->grp;
@@ -462,8 +466,12 @@ static bool plan_ts(const sc_conv_config* c, sc_dtype dt, const sc_epilogue& e, 
     const char* te_env = std::getenv("SC_TS_TMAEPI");
     plan->tma_epi = (te_env ? te_env[0] == '1' : plan->n_buf == 1) && tile_n % 64 == 0 ? 1 : 0;
     // double-buffered staging with >= 3 weight stages if it fits, else single-buffered staging
-    for (int ns = 2; ns >= 1; --ns) {
-        int S = 12;
+    // (tuning: SC_TS_NSTG=1 forces single-buffered staging, SC_TS_SMAX caps the weight stages, <= 16)
+    const char* ns_env = std::getenv("SC_TS_NSTG");
+    const char* smax_env = std::getenv("SC_TS_SMAX");
+    const int s_max = smax_env ? std::max(2, std::min(16, std::atoi(smax_env))) : 12;
+    for (int ns = (ns_env && ns_env[0] == '1') ? 1 : 2; ns >= 1; --ns) {
+        int S = s_max;
         while (S >= 2 && ts_smem_bytes(plan->u_cap, tile_n, (int)K, S, ns, plan->tma_epi) > kMaxDynSmem) --S;
         S = S / plan->grp * plan->grp;  // whole slot groups
         if (S >= 2 * plan->grp) {
