@@ -73,12 +73,17 @@ class ResBlockStack:
         return 2 * len(self.blocks)
 
     def forward(self, x: torch.Tensor, nbr: torch.Tensor, bufs: dict | None = None,
-                schedule: "F.ConvSchedule | None" = None) -> torch.Tensor:
+                schedule: "F.ConvSchedule | None" = None, h0: torch.Tensor | None = None) -> torch.Tensor:
         """x [N, C] (bf16 or f32) -> [N, C]; ``nbr`` is the [N, 27] map;
-        ``schedule`` (optional) its conv schedule (F.neighbor_schedule)."""
+        ``schedule`` (optional) its conv schedule (F.neighbor_schedule); ``h0``
+        (optional) SiLU(LN1(x)) of the first block, already computed by the
+        producer of x (e.g. the upsample's conv2 epilogue), in a buffer the
+        stack may overwrite."""
         n, c = x.shape
         if bufs is None:
             bufs = {}
+        if h0 is not None:
+            bufs["h"] = h0
         def buf(name):
             t = bufs.get(name)
             if t is None or t.shape != x.shape or t.dtype != x.dtype:
@@ -86,7 +91,7 @@ class ResBlockStack:
                 bufs[name] = t
             return t
         b0 = self.blocks[0]
-        h = F.layer_norm_affine_silu_forward(x, b0.ln1_g, b0.ln1_b, b0.eps, out=buf("h"))
+        h = h0 if h0 is not None else F.layer_norm_affine_silu_forward(x, b0.ln1_g, b0.ln1_b, b0.eps, out=buf("h"))
         cur = x
         ping = [buf("x0"), buf("x1")]
         for i, p in enumerate(self.blocks):
@@ -137,14 +142,16 @@ class C2SUpsampleBlock:
         self.schedule_children = True
 
     def forward(self, coords: torch.Tensor, x: torch.Tensor, mask: torch.Tensor | None = None, nbr_parent=None,
-                threshold: float = 0.0, keep: dict | None = None):
+                threshold: float = 0.0, keep: dict | None = None, next_ln=None):
         """Returns (child_coords, child_feats, child_nbr).  Without ``mask`` the
         children come from the to_subdiv head on x (logits > threshold).  With
         ``keep`` (a dict) the intermediates are left in it: ``h`` (parents after
         LN + SiLU), ``h_up`` (children after conv1's LN + SiLU epilogue),
         ``child_row`` ([Np, 8] child of each parent block), ``nbr_parent``,
         ``sched_child`` (the child map's conv schedule, for the convs that
-        follow on the children; None when ``schedule_children`` is off)."""
+        follow on the children; None when ``schedule_children`` is off) and,
+        with ``next_ln`` = (gamma, beta, eps) of the block that follows,
+        ``h_next`` = SiLU(LN(y)) emitted by conv2's epilogue as a second output."""
         p = self.p
         if mask is None:
             if p.w_sub is None:
@@ -173,11 +180,18 @@ class C2SUpsampleBlock:
         # halves the executed MMA work of conv2 and of the ResBlock convs that follow
         sched2 = F.neighbor_schedule(self.cfg2, nbr_child) if self.schedule_children and n_child else None
         rep = self.cout // (self.cin // 8)
-        y = F.sparse_subm_conv_forward(
-            self.cfg2, h_up, nbr_child, p.w2, p.b2,
-            F.Epilogue(residual=x, residual_offset=skip_off, residual_repeat=rep, schedule=sched2))
+        h_next = None
+        if next_ln is not None:
+            g, be, eps = next_ln
+            h_next = torch.empty((n_child, self.cout), dtype=x.dtype, device=x.device)
+            e2 = F.Epilogue(residual=x, residual_offset=skip_off, residual_repeat=rep, schedule=sched2,
+                            layer_norm=True, ln_eps=eps, ln_gamma=g, ln_beta=be, silu=True, out2=h_next)
+        else:
+            e2 = F.Epilogue(residual=x, residual_offset=skip_off, residual_repeat=rep, schedule=sched2)
+        y = F.sparse_subm_conv_forward(self.cfg2, h_up, nbr_child, p.w2, p.b2, e2)
         if keep is not None:
-            keep.update(h=h, h_up=h_up, child_row=child_row, nbr_parent=nbr_parent, sched_child=sched2)
+            keep.update(h=h, h_up=h_up, child_row=child_row, nbr_parent=nbr_parent, sched_child=sched2,
+                        h_next=h_next)
         return child_coords, y, nbr_child
 
     def flops(self, nbr_parent: torch.Tensor, nbr_child: torch.Tensor, mask: torch.Tensor) -> float:
@@ -202,9 +216,13 @@ class UpsamplePyramid:
 
     def forward(self, coords: torch.Tensor, x: torch.Tensor, masks: list[torch.Tensor]):
         stats = []
+        nbr = None  # a level's child map is the next level's parent map (same 3x3x3 geometry)
         for (c2s, res, _), mask in zip(self.levels, masks):
             keep: dict = {}
-            coords, x, nbr = c2s.forward(coords, x, mask, keep=keep)
+            # (emitting the first ResBlock's SiLU(LN1(.)) from conv2's epilogue instead of the row
+            # kernel measured no faster on config 3: conv2 with the LayerNorm epilogue took
+            # 0.04-0.14 ms longer a level, about what the row kernel costs)
+            coords, x, nbr = c2s.forward(coords, x, mask, nbr_parent=nbr, keep=keep)
             x = res.forward(x, nbr, schedule=keep["sched_child"])
             stats.append((coords.shape[0], nbr))
         return coords, x, stats
