@@ -51,6 +51,25 @@ def test_c2s_block(cuda_device, cin, cout):
     assert_no_fault()
 
 
+def test_c2s_conv2_emits_next_layer_norm(cuda_device):
+    """With next_ln, the upsample's conv2 epilogue also writes SiLU(LN(y)) (the first
+    ResBlock's input) as a second output: equal to the row kernel run on y."""
+    coords = shell(grid=24, r=8.0)
+    n = coords.shape[0]
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((n, 192)).astype(np.float32)
+    p = synth.c2s_params(rng, 192, 96)
+    mask = synth.child_mask(9, n)
+    blk = blocks.C2SUpsampleBlock(blocks.C2SParams.from_numpy(p, dev()))
+    g = torch.as_tensor((1 + 0.1 * rng.standard_normal(96)).astype(np.float32), device=dev())
+    be = torch.as_tensor((0.1 * rng.standard_normal(96)).astype(np.float32), device=dev())
+    keep = {}
+    _, y, _ = blk.forward(to_dev(coords), to_dev(x, torch.bfloat16), to_dev(mask), keep=keep, next_ln=(g, be, 1e-5))
+    ref = F.layer_norm_affine_silu_forward(y, g, be, 1e-5)
+    assert rel_l2(keep["h_next"].float().cpu().numpy(), ref.float().cpu().numpy()) <= 1e-2
+    assert_no_fault()
+
+
 @pytest.mark.parametrize("n_keep", ["random", "none", "all"])
 def test_subdivide_async_matches_sync(cuda_device, n_keep):
     """sc_subdivide_async leaves the child count on the device and writes the same child rows,
