@@ -51,6 +51,9 @@ CPU_ROWS_PER_CALL = 8192
 CPU_WINDOW_ROWS = 65536
 
 
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -431,12 +434,19 @@ def main():
             "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded; BASELINE shapes and distributions)",
             "tflops": flops / t_dev / 1e12, "pct_bf16_peak": flops / t_dev / 1e12 / (peak_tf * world),
             "config": cfgd,
-            "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
-                         "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
-                         "frac_of_sustained": (achieved / peak_sus) if peak_sus else None,
-                         "peak_source": f"{peak_kind} bf16 (burst); frac_of_sustained against the sustained figure",
-                         "traffic": read_traffic(args.workload),
-                         "flops_per_step_rank0": wl.flops, "conv_ms_per_step_rank0": conv_ms_step},
+            "roofline": ({"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": achieved,
+                          "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                          "frac_of_sustained": (achieved / peak_sus) if peak_sus else None,
+                          "peak_source": f"{peak_kind} bf16 (burst); frac_of_sustained against the sustained figure",
+                          "traffic": read_traffic(args.workload),
+                          "flops_per_step_rank0": wl.flops, "conv_ms_per_step_rank0": conv_ms_step}
+                         if wl.dtype != "f32" else
+                         # fp32 runs on the CUDA cores: no measured FP32 peak exists, so the nominal FFMA
+                         # peak at the maximum SM clock (148 SMs x 128 FMA/clock x 2 x 1.965 GHz)
+                         {"bound": "fp32", "kernel": "conv_f32_tiled_kernel", "achieved": achieved,
+                          "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s", "frac": achieved / FP32_NOMINAL_TFLOPS,
+                          "frac_of_sustained": None, "peak_source": "nominal FP32 FFMA peak (no measured figure)",
+                          "traffic": None, "flops_per_step_rank0": wl.flops, "conv_ms_per_step_rank0": conv_ms_step}),
             "cpu_baseline": cpu,
             "e2e": ({"value": units / t_e2e, "unit": "voxel-outputs/s", "h2d_bytes_per_step": h2d * world,
                      "d2h_bytes_per_step": d2h * world} if t_e2e else None),
