@@ -29,7 +29,7 @@ EXPORTED = (
     "sc_neighbor_workspace_bytes", "sc_neighbor_map", "sc_neighbor_map_query", "sc_neighbor_status",
     "sc_neighbor_map_noalloc", "sc_neighbor_schedule_scratch_bytes", "sc_neighbor_schedule",
     "sc_subm_conv_forward", "sc_conv_uses_tensor_cores", "sc_layer_norm_act", "sc_bf16_round",
-    "sc_cast", "sc_subdivide_scratch_bytes", "sc_subdivide", "sc_subdivide_async", "sc_gather_rows", "sc_subdiv_head",
+    "sc_cast", "sc_subdivide_scratch_bytes", "sc_subdivide", "sc_subdivide_async", "sc_linear_forward", "sc_gather_rows", "sc_subdiv_head",
     "sc_patchify3d_scratch_bytes", "sc_patchify3d_forward", "sc_neighbor_schedule_grouped_scratch_bytes",
     "sc_neighbor_schedule_grouped", "sc_set_wait_limit_ns", "sc_neighbor_tile_sources_bytes",
     "sc_neighbor_tile_sources",
@@ -118,6 +118,7 @@ _SIGS = {
     "sc_subdivide_scratch_bytes": ([_I64, ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "sc_subdivide": ([_P, _P, _I64, _I64, _P, _P, _P, _P, ctypes.POINTER(ctypes.c_int64), _P], ctypes.c_int),
     "sc_subdivide_async": ([_P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P], ctypes.c_int),
+    "sc_linear_forward": ([ctypes.c_int, _P, _I64, _I64, _P, _I64, _P, _P, ctypes.c_int32, _P, _P], ctypes.c_int),
 }
 
 

@@ -19,6 +19,7 @@
 #include "conv_simt.cuh"
 #include "conv_tc.cuh"
 #include "conv_ts.cuh"
+#include "linear_tc.cuh"
 #include "neighbor.cuh"
 #include "rowops.cuh"
 #include "sc_common.cuh"
@@ -988,6 +989,72 @@ int sc_layer_norm_act(sc_dtype dtype, const void* x, int64_t rows, int64_t chann
     return SC_OK;
 }
 
+int sc_linear_forward(sc_dtype dtype, const void* x, int64_t rows, int64_t cin, const void* w, int64_t cout,
+                      const float* bias, const void* residual, int32_t silu, void* out, void* stream) {
+    if (rows < 0 || cin <= 0 || cout <= 0) return fail(SC_ERR_INVALID, "invalid linear shape");
+    if (rows == 0) return SC_OK;
+    if (!x || !w || !out) return fail(SC_ERR_INVALID, "null pointer");
+    if (dtype != SC_DTYPE_BF16 || force_simt()) return fail(SC_ERR_UNSUPPORTED, "linear: bf16 tensor-core path only");
+    if (const char* env = std::getenv("SC_LINEAR_TC"))
+        if (env[0] == '0') return fail(SC_ERR_UNSUPPORTED, "linear: tensor-core path switched off");
+    if (cin % 8 != 0 || cout % 32 != 0) return fail(SC_ERR_UNSUPPORTED, "linear: needs in % 8 == 0, out % 32 == 0");
+    if (rows > 0x7fffff00LL) return fail(SC_ERR_UNSUPPORTED, "linear: too many rows");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(out) || !aligned16(bias) || !aligned16(residual))
+        return fail(SC_ERR_UNSUPPORTED, "linear: pointers must be 16-byte aligned");
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    // column tile: all outputs up to 256, else the smallest split into equal multiples of 32 <= 256;
+    // halved while the grid has fewer tiles than SMs (as the conv planner does)
+    int64_t ny = (cout + 255) / 256;
+    while (cout % ny != 0 || (cout / ny) % 32 != 0) ++ny;
+    int tile_n = (int)(cout / ny);
+    const int64_t row_tiles = (rows + 127) / 128;
+    while (row_tiles * (cout / tile_n) < sm_count() && tile_n >= 128 && (tile_n / 2) % 32 == 0 &&
+           cout % (tile_n / 2) == 0)
+        tile_n /= 2;
+    int S = 8;
+    while (S > 2 && lin_smem_bytes(tile_n, S) > kMaxDynSmem) --S;
+    CUtensorMap amap, bmap;
+    cuuint64_t ad[2] = {(cuuint64_t)cin, (cuuint64_t)rows};
+    cuuint64_t bd[2] = {(cuuint64_t)cin, (cuuint64_t)cout};
+    cuuint64_t st[1] = {(cuuint64_t)cin * 2};
+    cuuint32_t abox[2] = {64u, 128u};
+    cuuint32_t bbox[2] = {64u, (cuuint32_t)tile_n};
+    cuuint32_t es[2] = {1u, 1u};
+    CUresult r1 = enc(&amap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), ad, st, abox, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r2 = enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w), bd, st, bbox, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled (linear) failed");
+    LinParams p;
+    memset(&p, 0, sizeof p);
+    p.rows = rows;
+    p.cin = (int)cin;
+    p.cout = (int)cout;
+    p.tile_n = tile_n;
+    p.grid_y = (int)(cout / tile_n);
+    p.n_tiles = row_tiles * p.grid_y;
+    p.stages = S;
+    p.bias = bias;
+    p.residual = static_cast<const __nv_bfloat16*>(residual);
+    p.silu = silu;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    static std::once_flag lin_once;
+    static cudaError_t lin_err = cudaSuccess;
+    std::call_once(lin_once, [] {
+        lin_err = cudaFuncSetAttribute((const void*)linear_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kMaxDynSmem);
+    });
+    SC_CUDA_TRY(lin_err);
+    const int64_t ctas = std::min<int64_t>(p.n_tiles, sm_count());
+    linear_tc_kernel<<<(unsigned)ctas, LIN_THREADS, lin_smem_bytes(tile_n, S), static_cast<cudaStream_t>(stream)>>>(
+        amap, bmap, p);
+    SC_CUDA_TRY(cudaGetLastError());
+    return SC_OK;
+}
+
 int sc_gather_rows(const void* src, int64_t n_src, int64_t row_bytes, const int32_t* idx, int64_t n, void* dst,
                    void* stream) {
     if (n < 0 || n_src < 0 || row_bytes <= 0) return fail(SC_ERR_INVALID, "invalid gather shape");
@@ -1109,7 +1176,12 @@ int sc_patchify3d_forward(const sc_patchify3d_config* c, sc_dtype dtype, const v
             static_cast<const __nv_bfloat16*>(input), reinterpret_cast<const int4*>(coords), rows, g,
             static_cast<__nv_bfloat16*>(cols));
     SC_CUDA_TRY(cudaGetLastError());
-    // projection: a 1x1x1 conv over the identity rows, weight [Cout, 1, 1, 1, K]
+    // projection: the dense tensor-core linear where it applies, else a 1x1x1 conv over the
+    // identity rows, weight [Cout, 1, 1, 1, K] = [Cout, K]
+    {
+        const int rc = sc_linear_forward(dtype, cols, rows, K, weight, c->out_channels, bias, nullptr, 0, out, stream);
+        if (rc != SC_ERR_UNSUPPORTED) return rc;
+    }
     sc_conv_config cc;
     memset(&cc, 0, sizeof cc);
     cc.in_channels = K;

@@ -409,6 +409,27 @@ def linear_forward(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor
     if bias is not None and bias.shape[0] != cout:
         raise SparseConvError(_lib.SC_ERR_INVALID,
                               f"linear: bias len {bias.shape[0]} does not match out_channels {cout}")
+    e = epilogue or Epilogue()
+    if (input.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and not e.layer_norm and e.out2 is None
+            and e.out_row_map is None and e.residual_offset is None and e.schedule is None
+            and e.tile_sources is None and (e.residual is None or (e.residual.shape == (rows, cout)
+                                                                   and e.residual.dtype == torch.bfloat16))):
+        # the dense tensor-core linear (sc_linear_forward); it declines shapes it does not take
+        y = out if out is not None else torch.empty((rows, cout), dtype=input.dtype, device=input.device)
+        res = e.residual.contiguous() if e.residual is not None else None
+        obs = _CONV_OBSERVER
+        lcfg = SparseSubmConvConfig(cin, cout, 1, 1, 1)
+        if obs is not None:
+            obs.before(lcfg, rows)
+        rc = lib().sc_linear_forward(_DT[input.dtype], _ptr(input.contiguous()), rows, cin,
+                                     _ptr(weight.contiguous()), cout, _ptr(bias), _ptr(res), int(e.silu), _ptr(y),
+                                     _stream(input))
+        if rc == _lib.SC_OK:
+            if obs is not None:
+                obs.after(lcfg, rows)
+            return y
+        if rc != _lib.SC_ERR_UNSUPPORTED:
+            check(rc)
     cfg = SparseSubmConvConfig(cin, cout, 1, 1, 1)
     return sparse_subm_conv_forward(cfg, input, identity_rows(rows, input.device),
                                     weight.reshape(cout, 1, 1, 1, cin), bias, epilogue, out=out)

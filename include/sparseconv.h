@@ -269,6 +269,21 @@ int sc_subdivide_async(const int32_t* d_parent_coords, const uint8_t* d_mask, in
                        int64_t* d_skip_offset /* [8*n_parent] */, int32_t* d_children,
                        void* stream);
 
+/* ---- dense linear layer ---------------------------------------------------
+ * out[r, o] = act(bias[o] + sum_c x[r, c] * W[o, c] (+ residual[r, o])) for
+ * bf16 x [rows, cin], W [cout, cin] (PyTorch linear layout), fp32 bias
+ * (nullable), bf16 residual [rows, cout] (nullable), act = SiLU when silu != 0
+ * (the order of sc_subm_conv_forward's epilogue).  Replaces burn_trellis linear_forward
+ * (runtime_model/sparse_decoder_wgpu_ops.rs:1-60) and the ConvNeXt MLP's two
+ * layers (:355-489).  Both operands arrive by TMA tiles (no neighbor map).
+ * Needs cin % 8 == 0, cout % 32 == 0 and 16-byte aligned pointers; returns
+ * SC_ERR_UNSUPPORTED otherwise (or with SC_FORCE_SIMT / SC_LINEAR_TC=0 set),
+ * and the caller runs the layer as a 1x1x1 sc_subm_conv_forward over the
+ * identity map. */
+int sc_linear_forward(sc_dtype dtype, const void* d_x, int64_t rows, int64_t in_features, const void* d_weight,
+                      int64_t out_features, const float* d_bias, const void* d_residual, int32_t silu,
+                      void* d_out, void* stream);
+
 /* ---- subdivision head (decoder upsample without a guide) -----------------
  * logits[n, 8] = feats[n, C] @ weight[8, C]^T + bias (the to_subdiv linear
  * layer; weight in feats' dtype, bias fp32, fp32 accumulate), optionally

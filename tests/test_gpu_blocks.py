@@ -164,6 +164,36 @@ def test_linear_forward(cuda_device, rows, cin, cout, dtype, tol):
     assert_no_fault()
 
 
+@pytest.mark.parametrize("rows,cin,cout,silu,residual", [(5000, 256, 1024, True, False), (3000, 1024, 256, False, True),
+                                                       (777, 72, 96, True, True), (100, 64, 64, False, False),
+                                                       (70000, 256, 768, True, False)])
+def test_dense_linear_matches_conv_route(cuda_device, monkeypatch, rows, cin, cout, silu, residual):
+    """The dense tensor-core linear (sc_linear_forward: TMA tiles, no map) against the same
+    layer as a 1x1x1 conv over the identity map (SC_LINEAR_TC=0) and against the oracle:
+    partial row tiles, a partial 64-channel chunk (72), split output tiles (768, 1024),
+    SiLU and the residual add."""
+    rng = np.random.default_rng(rows + cin)
+    x = rng.standard_normal((rows, cin)).astype(np.float32)
+    w = (0.05 * rng.standard_normal((cout, cin))).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    r = rng.standard_normal((rows, cout)).astype(np.float32)
+    xd, wd, bd = to_dev(x, torch.bfloat16), to_dev(w, torch.bfloat16), to_dev(b)
+    rd = to_dev(r, torch.bfloat16) if residual else None
+    epi = F.Epilogue(silu=silu, residual=rd)
+    dense = F.linear_forward(xd, wd, bd, epi)
+    monkeypatch.setenv("SC_LINEAR_TC", "0")
+    conv = F.linear_forward(xd, wd, bd, epi)
+    monkeypatch.delenv("SC_LINEAR_TC")
+    assert rel_l2(dense.float().cpu().numpy(), conv.float().cpu().numpy()) <= 1e-6
+    ref = OB.linear(x, w, b, bf16=True)
+    if residual:
+        ref = ref + oracle.bf16_round(r)
+    if silu:
+        ref = oracle.silu(ref)
+    assert rel_l2(dense.float().cpu().numpy(), oracle.bf16_round(ref)) <= 1e-2
+    assert_no_fault()
+
+
 def test_linear_forward_errors(cuda_device):
     x = to_dev(np.zeros((4, 64), np.float32), torch.bfloat16)
     with pytest.raises(F.SparseConvError, match="invalid input len"):
