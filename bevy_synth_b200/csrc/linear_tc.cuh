@@ -12,9 +12,10 @@
 //   0    TMA producer (one lane): A and B of every 64-channel stage;
 //   1    MMA issuer (whole warp runs the loop, one elected lane issues
 //        tcgen05.mma M=128, N, K=16) and TMEM owner;
-//   2-5  epilogue: thread = tile row (TMEM lane), 32 columns at a time:
-//        + bias, [+ residual], [SiLU], bf16 16-byte stores (the conv
-//        epilogue's order).
+//   2-9  epilogue, two warps per TMEM sub-partition: thread = tile row
+//        (TMEM lane), 64-column boxes: + bias, [+ residual], [SiLU] (the
+//        conv epilogue's order), bf16 into a swizzled staging box, one TMA
+//        tile store per box.
 // TMEM: two accumulators of N <= 256 columns, so a tile's epilogue overlaps
 // the next tile's MMAs.  Every wait is bounded (device wait limit); on expiry
 // the fault word is raised and the roles drain.
@@ -24,7 +25,9 @@
 
 namespace sc {
 
-constexpr int LIN_THREADS = 6 * 32;
+constexpr int LIN_EPI_WARPS = 8;                 // two per TMEM sub-partition
+constexpr int LIN_THREADS = (2 + LIN_EPI_WARPS) * 32;
+constexpr int LIN_EPI_BYTES = LIN_EPI_WARPS * 32 * 128;  // one 32-row x 64-column bf16 box per warp
 constexpr int LIN_A_BYTES = 128 * 128;  // 128 rows x 64 bf16
 
 struct LinParams {
@@ -51,11 +54,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* desc, uint
 }
 
 inline size_t lin_smem_bytes(int tile_n, int stages) {
-    return 1024 + (size_t)stages * (LIN_A_BYTES + (size_t)tile_n * 128) + (size_t)(2 * stages + 4) * 8 + 16;
+    return 1024 + (size_t)stages * (LIN_A_BYTES + (size_t)tile_n * 128) + LIN_EPI_BYTES +
+           (size_t)(2 * stages + 4) * 8 + 16;
 }
 
 __global__ void __launch_bounds__(LIN_THREADS, 1) linear_tc_kernel(const __grid_constant__ CUtensorMap amap,
                                                                    const __grid_constant__ CUtensorMap bmap,
+                                                                   const __grid_constant__ CUtensorMap omap,
                                                                    const LinParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -64,7 +69,8 @@ __global__ void __launch_bounds__(LIN_THREADS, 1) linear_tc_kernel(const __grid_
     const int B_BYTES = p.tile_n * 128;
     uint8_t* a_smem = smem;                                    // [S][128 rows][128 B]
     uint8_t* b_smem = a_smem + (size_t)S * LIN_A_BYTES;        // [S][tile_n rows][128 B]
-    uint64_t* full = reinterpret_cast<uint64_t*>(b_smem + (size_t)S * B_BYTES);
+    uint8_t* epi_s = b_smem + (size_t)S * B_BYTES;             // [8 warps][32 rows][128 B], 1024-aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi_s + LIN_EPI_BYTES);
     uint64_t* empty = full + S;
     uint64_t* tmem_full = empty + S;   // [2]
     uint64_t* tmem_empty = tmem_full + 2;  // [2]
@@ -86,7 +92,7 @@ __global__ void __launch_bounds__(LIN_THREADS, 1) linear_tc_kernel(const __grid_
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tmem_full[b], 1);   // tcgen05.commit after a tile's last MMA
-            mbar_init(&tmem_empty[b], 4);  // the four epilogue warps
+            mbar_init(&tmem_empty[b], LIN_EPI_WARPS);  // every epilogue warp
         }
         fence_mbar_init();
         fence_proxy_async_smem();
@@ -174,7 +180,15 @@ __global__ void __launch_bounds__(LIN_THREADS, 1) linear_tc_kernel(const __grid_
         }
     } else {
         // ====================================================== epilogue
-        const int q = warp & 3;  // TMEM sub-partition of this warp (warps 2..5 -> 2, 3, 0, 1)
+        // Two warps per TMEM sub-partition: warp e (= warp - 2) reads lanes 32 (e % 4) .. + 31
+        // and the 64-column boxes h, h + 2, ... (h = e / 4) of the tile.  A box goes out through
+        // this warp's 128B-swizzled 4 KB staging and one TMA tile store (whole 128-byte lines;
+        // rows past the end are not written); the next box waits until that store has read the
+        // staging.  The accumulator is released once every warp has its last columns.
+        const int e = warp - 2;
+        const int q = warp & 3;  // TMEM sub-partition of this warp
+        const int h = e >> 2;
+        uint8_t* es = epi_s + (size_t)e * 32 * 128;
         for (int64_t lt = 0;; ++lt) {
             const int64_t t = tile_of(lt);
             if (t < 0) break;
@@ -182,42 +196,53 @@ __global__ void __launch_bounds__(LIN_THREADS, 1) linear_tc_kernel(const __grid_
             const uint32_t use = (uint32_t)(lt >> 1);
             if (!__all_sync(0xffffffffu, mbar_wait(&tmem_full[b], use & 1u))) break;
             tc_fence_after();
-            const int64_t row = (t / p.grid_y) * 128 + q * 32 + lane;
+            const int64_t row0 = (t / p.grid_y) * 128 + q * 32;
+            const int64_t row = row0 + lane;
             const int n0 = (int)(t % p.grid_y) * p.tile_n;
             const uint32_t lane_addr = tmem_base + (uint32_t)(b * p.tile_n) + ((uint32_t)(q * 32) << 16);
             const bool live = row < p.rows;
-            uint8_t* dst = reinterpret_cast<uint8_t*>(p.out + (live ? row : 0) * (int64_t)p.cout + n0);
             const uint8_t* res = p.residual
                 ? reinterpret_cast<const uint8_t*>(p.residual + (live ? row : 0) * (int64_t)p.cout + n0)
                 : nullptr;
-            for (int c = 0; c < p.tile_n; c += 32) {
-                float v[32];
-                tmem_ld32(lane_addr + c, v);
-                if (c + 32 >= p.tile_n) {  // the accumulator is free once its last columns are in registers
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tmem_empty[b]);
-                }
-                if (p.bias) add_param32(v, p.bias + n0 + c, false);
-                if (live) {
-                    if (res) {
+            const int n_box = p.tile_n / 64;
+            for (int bx = h; bx < n_box; bx += 2) {
+                if (lane == 0) bulk_wait_read_all();  // the previous box's store has read the staging
+                __syncwarp();
+#pragma unroll 1
+                for (int half = 0; half < 2; ++half) {
+                    const int c = bx * 64 + half * 32;
+                    float v[32];
+                    tmem_ld32(lane_addr + c, v);
+                    if (p.bias) add_param32(v, p.bias + n0 + c, false);
+                    if (res && live) {
 #pragma unroll
                         for (int qq = 0; qq < 4; ++qq) {
                             float r[8];
                             load_bf16x8(res + (c + 8 * qq) * 2, r);
 #pragma unroll
-                            for (int e = 0; e < 8; ++e) v[8 * qq + e] += r[e];
+                            for (int k = 0; k < 8; ++k) v[8 * qq + k] += r[k];
                         }
                     }
                     if (p.silu) {
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) v[e] = silu_bf16out(v[e]);
+                        for (int k = 0; k < 32; ++k) v[k] = silu_bf16out(v[k]);
                     }
 #pragma unroll
-                    for (int qq = 0; qq < 4; ++qq) cvt_store_bf16x8(dst + (c + 8 * qq) * 2, v + 8 * qq);
+                    for (int u = 0; u < 4; ++u)
+                        cvt_store_bf16x8(es + lane * 128 + (((4 * half + u) ^ (lane & 7)) << 4), v + 8 * u);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&omap, smem_u32(es), n0 + bx * 64, (int)row0);
+                    bulk_commit();
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[b]);
         }
+        if (lane == 0) bulk_wait_all();  // every output box written before the CTA leaves
     }
 
     tc_fence_before();

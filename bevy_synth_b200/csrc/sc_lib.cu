@@ -997,19 +997,19 @@ int sc_linear_forward(sc_dtype dtype, const void* x, int64_t rows, int64_t cin, 
     if (dtype != SC_DTYPE_BF16 || force_simt()) return fail(SC_ERR_UNSUPPORTED, "linear: bf16 tensor-core path only");
     if (const char* env = std::getenv("SC_LINEAR_TC"))
         if (env[0] == '0') return fail(SC_ERR_UNSUPPORTED, "linear: tensor-core path switched off");
-    if (cin % 8 != 0 || cout % 32 != 0) return fail(SC_ERR_UNSUPPORTED, "linear: needs in % 8 == 0, out % 32 == 0");
+    if (cin % 8 != 0 || cout % 64 != 0) return fail(SC_ERR_UNSUPPORTED, "linear: needs in % 8 == 0, out % 64 == 0");
     if (rows > 0x7fffff00LL) return fail(SC_ERR_UNSUPPORTED, "linear: too many rows");
     if (!aligned16(x) || !aligned16(w) || !aligned16(out) || !aligned16(bias) || !aligned16(residual))
         return fail(SC_ERR_UNSUPPORTED, "linear: pointers must be 16-byte aligned");
     EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-    // column tile: all outputs up to 256, else the smallest split into equal multiples of 32 <= 256;
-    // halved while the grid has fewer tiles than SMs (as the conv planner does)
+    // column tile: all outputs up to 256, else the smallest split into equal multiples of 64 <= 256
+    // (the epilogue stores 64-column boxes); halved while the grid has fewer tiles than SMs
     int64_t ny = (cout + 255) / 256;
-    while (cout % ny != 0 || (cout / ny) % 32 != 0) ++ny;
+    while (cout % ny != 0 || (cout / ny) % 64 != 0) ++ny;
     int tile_n = (int)(cout / ny);
     const int64_t row_tiles = (rows + 127) / 128;
-    while (row_tiles * (cout / tile_n) < sm_count() && tile_n >= 128 && (tile_n / 2) % 32 == 0 &&
+    while (row_tiles * (cout / tile_n) < sm_count() && tile_n >= 128 && (tile_n / 2) % 64 == 0 &&
            cout % (tile_n / 2) == 0)
         tile_n /= 2;
     int S = 8;
@@ -1027,7 +1027,14 @@ int sc_linear_forward(sc_dtype dtype, const void* x, int64_t rows, int64_t cin, 
     CUresult r2 = enc(&bmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w), bd, st, bbox, es,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled (linear) failed");
+    CUtensorMap omap;
+    cuuint64_t od[2] = {(cuuint64_t)cout, (cuuint64_t)rows};
+    cuuint64_t ost[1] = {(cuuint64_t)cout * 2};
+    cuuint32_t obox[2] = {64u, 32u};
+    CUresult r3 = enc(&omap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, od, ost, obox, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS || r3 != CUDA_SUCCESS)
+        return fail(SC_ERR_CUDA, "cuTensorMapEncodeTiled (linear) failed");
     LinParams p;
     memset(&p, 0, sizeof p);
     p.rows = rows;
@@ -1050,7 +1057,7 @@ int sc_linear_forward(sc_dtype dtype, const void* x, int64_t rows, int64_t cin, 
     SC_CUDA_TRY(lin_err);
     const int64_t ctas = std::min<int64_t>(p.n_tiles, sm_count());
     linear_tc_kernel<<<(unsigned)ctas, LIN_THREADS, lin_smem_bytes(tile_n, S), static_cast<cudaStream_t>(stream)>>>(
-        amap, bmap, p);
+        amap, bmap, omap, p);
     SC_CUDA_TRY(cudaGetLastError());
     return SC_OK;
 }

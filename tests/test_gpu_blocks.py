@@ -165,13 +165,14 @@ def test_linear_forward(cuda_device, rows, cin, cout, dtype, tol):
 
 
 @pytest.mark.parametrize("rows,cin,cout,silu,residual", [(5000, 256, 1024, True, False), (3000, 1024, 256, False, True),
-                                                       (777, 72, 96, True, True), (100, 64, 64, False, False),
-                                                       (70000, 256, 768, True, False)])
+                                                       (777, 72, 128, True, True), (100, 64, 64, False, False),
+                                                       (70000, 256, 768, True, False),
+                                                       (500, 64, 96, True, False)])
 def test_dense_linear_matches_conv_route(cuda_device, monkeypatch, rows, cin, cout, silu, residual):
     """The dense tensor-core linear (sc_linear_forward: TMA tiles, no map) against the same
     layer as a 1x1x1 conv over the identity map (SC_LINEAR_TC=0) and against the oracle:
     partial row tiles, a partial 64-channel chunk (72), split output tiles (768, 1024),
-    SiLU and the residual add."""
+    SiLU and the residual add; 96 outputs (not a multiple of 64) take the conv route."""
     rng = np.random.default_rng(rows + cin)
     x = rng.standard_normal((rows, cin)).astype(np.float32)
     w = (0.05 * rng.standard_normal((cout, cin))).astype(np.float32)
