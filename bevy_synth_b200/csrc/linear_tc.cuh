@@ -206,9 +206,16 @@ __global__ void __launch_bounds__(LIN_THREADS, 1) linear_tc_kernel(const __grid_
                 : nullptr;
             const int n_box = p.tile_n / 64;
             for (int bx = h; bx < n_box; bx += 2) {
+                // the box's residual (64 values of this row) is loaded up front, so its latency
+                // overlaps the TMEM loads and the staging wait
+                uint4 rbox[8];
+                if (res && live) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) rbox[i] = __ldg(reinterpret_cast<const uint4*>(res + bx * 128) + i);
+                }
                 if (lane == 0) bulk_wait_read_all();  // the previous box's store has read the staging
                 __syncwarp();
-#pragma unroll 1
+#pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     const int c = bx * 64 + half * 32;
                     float v[32];
@@ -218,7 +225,7 @@ __global__ void __launch_bounds__(LIN_THREADS, 1) linear_tc_kernel(const __grid_
 #pragma unroll
                         for (int qq = 0; qq < 4; ++qq) {
                             float r[8];
-                            load_bf16x8(res + (c + 8 * qq) * 2, r);
+                            load_bf16x8(reinterpret_cast<const uint8_t*>(&rbox[4 * half + qq]), r);
 #pragma unroll
                             for (int k = 0; k < 8; ++k) v[8 * qq + k] += r[k];
                         }
