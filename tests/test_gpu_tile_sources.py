@@ -85,6 +85,33 @@ def test_tile_source_conv_equals_generic_kernel(cuda_device, monkeypatch, cout, 
     assert_no_fault()
 
 
+@pytest.mark.parametrize("env,cout", [({"SC_TS_WIDE": "1"}, 256), ({"SC_TS_WIDE": "2"}, 256),
+                                     ({"SC_TS_WIDE": "1", "SC_TS_TMAEPI": "0"}, 192),
+                                     ({"SC_TS_TMAEPI": "1"}, 64), ({"SC_TS_G": "2"}, 64),
+                                     ({"SC_TS_NSTG": "1", "SC_TS_SMAX": "16"}, 64)])
+def test_tile_source_variants_equal_generic_kernel(cuda_device, monkeypatch, env, cout):
+    """The opt-in tile-source variants (wide outputs with one single-buffered accumulator or
+    128-wide column tiles, the TMA box-store epilogue, the pipeline-shape switches) give the
+    generic kernel's result."""
+    coords = shell()
+    n = coords.shape[0]
+    rng = np.random.default_rng(cout + len(env))
+    x = rng.standard_normal((n, 64)).astype(np.float32)
+    w = (0.05 * rng.standard_normal((cout, 3, 3, 3, 64))).astype(np.float32)
+    b = rng.standard_normal(cout).astype(np.float32)
+    cfg = F.SparseSubmConvConfig.subm3(64, cout)
+    nbr = F.neighbor_rows_tensor_from_coords_tensor(cfg, to_dev(coords))
+    ts = F.neighbor_tile_sources(cfg, nbr)
+    xd, wd, bd = to_dev(x, torch.bfloat16), to_dev(w, torch.bfloat16), to_dev(b)
+    monkeypatch.setenv("SC_TC_PAIR", "0")
+    ref_gpu = F.sparse_subm_conv_forward(cfg, xd, nbr, wd, bd, F.Epilogue())
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    got = F.sparse_subm_conv_forward(cfg, xd, nbr, wd, bd, F.Epilogue(tile_sources=ts))
+    assert rel_l2(got.float().cpu().numpy(), ref_gpu.float().cpu().numpy()) <= 1e-6
+    assert_no_fault()
+
+
 def test_plan_over_capacity_falls_back(cuda_device):
     """A map whose tiles read more distinct rows than the staging holds gives no plan; the conv
     then runs on the generic kernel."""
